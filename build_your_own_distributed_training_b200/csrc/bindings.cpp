@@ -1,0 +1,41 @@
+// Python bindings of the native extension.
+#include <torch/extension.h>
+
+void gemm_entry(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_mn, bool b_mn, int64_t epi,
+                c10::optional<torch::Tensor> R, c10::optional<torch::Tensor> alpha,
+                c10::optional<torch::Tensor> cos_t, c10::optional<torch::Tensor> sin_t,
+                c10::optional<torch::Tensor> D2, int64_t p0, int64_t p1);
+std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);
+torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw_acc);
+void rope_bwd(torch::Tensor d, torch::Tensor c, torch::Tensor s, int64_t rc, int64_t hd, int64_t sl);
+void rope_fwd(torch::Tensor d, torch::Tensor c, torch::Tensor s, int64_t rc, int64_t hd, int64_t sl);
+void swiglu_bwd(torch::Tensor da, torch::Tensor gu, torch::Tensor dgu);
+torch::Tensor embedding_fwd(torch::Tensor tok, torch::Tensor w, c10::ScalarType out_dtype);
+void embedding_bwd(torch::Tensor tok, torch::Tensor dout, torch::Tensor acc);
+std::vector<torch::Tensor> cross_entropy_fwd(torch::Tensor logits, torch::Tensor labels, int64_t ignore);
+void adamw(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, torch::Tensor out,
+           c10::optional<torch::Tensor> clip, double lr, double b1, double b2, double eps, double wd, int64_t step);
+torch::Tensor sumsq(torch::Tensor x);
+std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t B, int64_t S, int64_t nq, int64_t nkv, int64_t hd,
+                                    double scale);
+torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, int64_t B, int64_t S,
+                       int64_t nq, int64_t nkv, int64_t hd, double scale);
+int64_t device_error();
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels for B200-native 2-D parallel LLaMA training";
+  m.def("gemm", &gemm_entry, "tcgen05 GEMM with fused epilogues");
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("rope_bwd", &rope_bwd);
+  m.def("rope_fwd", &rope_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("embedding_fwd", &embedding_fwd);
+  m.def("embedding_bwd", &embedding_bwd);
+  m.def("cross_entropy_fwd", &cross_entropy_fwd);
+  m.def("adamw", &adamw);
+  m.def("sumsq", &sumsq);
+  m.def("attn_fwd", &attn_fwd);
+  m.def("attn_bwd", &attn_bwd);
+  m.def("device_error", &device_error, "read and clear the device error word");
+}

@@ -1,0 +1,542 @@
+// Persistent warp-specialised tcgen05 GEMM for sm_100a with fused epilogues.
+//
+//   C[M,N] = sum_k A(m,k) * B(n,k)      bf16 inputs, fp32 accumulation in TMEM
+//
+// A and B are each K-major (reduction axis contiguous) or MN-major, so the
+// three products of a linear layer (forward x.W^T, input grad dy.W, weight
+// grad dy^T.x) all run without transposing anything in memory.
+//
+// CTA = 6 warps, one CTA per SM, grid = min(#tiles, #SMs), static tile stride:
+//   warp 0      TMA producer: one elected thread streams 128x64 A and BNx64 B
+//               tiles (128-byte swizzle) into a STAGES-deep smem ring;
+//   warp 1      owns the TMEM allocation (2 x BN fp32 columns: the accumulator
+//               is double buffered) and one thread issues tcgen05.mma
+//               128xBNx16 instructions; tcgen05.commit releases smem stages
+//               and publishes finished accumulators;
+//   warps 2-5   epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
+//               32*(w%4)..+31 = tile rows), apply the fused epilogue and store,
+//               while the MMA warp already accumulates the next tile into the
+//               other TMEM buffer.
+//
+// Epilogues: bf16 / fp32 store (optional device-scalar alpha), fp32
+// accumulate into an existing buffer (weight gradients), residual add,
+// rotate-half RoPE on the q/k columns, and SwiGLU (B rows n and F+n of the
+// stacked [W_gate; W_up] land in one 256-wide tile, the epilogue writes
+// silu(g)*u plus g and u for the backward).
+//
+// No TMA multicast anywhere: each CTA loads its own tiles.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cudaTypedefs.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace dtb {
+
+enum Epi : int {
+  EPI_STORE_BF16 = 0,
+  EPI_STORE_F32 = 1,
+  EPI_ACC_F32 = 2,
+  EPI_RESIDUAL = 3,
+  EPI_ROPE = 4,
+  EPI_SWIGLU = 5,
+};
+
+struct GemmArgs {
+  int M, N, K;          // N: output columns (for SwiGLU: F)
+  void* D;
+  long ldd;
+  const __nv_bfloat16* R;
+  long ldr;
+  const float* alpha;
+  const float* cos_t;
+  const float* sin_t;
+  int rope_cols, head_dim, seqlen;
+  __nv_bfloat16* D2;
+  long ldd2;
+  int ffn;
+  int m_blocks, n_blocks, k_iters, num_tiles;
+  int* err;
+};
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int GROUP_M = 16;
+
+__device__ __forceinline__ void tile_coords(int tile, int mblocks, int nblocks, int& mb, int& nb) {
+  const int per_group = GROUP_M * nblocks;
+  const int g = tile / per_group;
+  const int first = g * GROUP_M;
+  const int gm = min(GROUP_M, mblocks - first);
+  const int r = tile - g * per_group;
+  mb = first + r % gm;
+  nb = r / gm;
+}
+
+template <int BN, int STAGES>
+struct SmemLayout {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 4) * 8 + 16 + 1024;  // + alignment slack
+};
+
+// ---------------------------------------------------------------- epilogue
+template <int EPI>
+__device__ __forceinline__ void store_chunk(const GemmArgs& a, int row, int col, float (&v)[32], int ncols_valid) {
+  if (a.alpha != nullptr) {
+    const float s = *a.alpha;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] *= s;
+  }
+  if (EPI == EPI_STORE_F32 || EPI == EPI_ACC_F32) {
+    float* p = reinterpret_cast<float*>(a.D) + (long)row * a.ldd + col;
+    if (ncols_valid >= 32) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        float4 o = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        if (EPI == EPI_ACC_F32) {
+          float4 c = *reinterpret_cast<float4*>(p + i);
+          o.x += c.x; o.y += c.y; o.z += c.z; o.w += c.w;
+        }
+        *reinterpret_cast<float4*>(p + i) = o;
+      }
+    } else {
+      for (int i = 0; i < ncols_valid; ++i) p[i] = (EPI == EPI_ACC_F32 ? p[i] : 0.f) + v[i];
+    }
+    return;
+  }
+  // bf16 outputs
+  __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(a.D) + (long)row * a.ldd + col;
+  if (EPI == EPI_RESIDUAL) {
+    const __nv_bfloat16* r = a.R + (long)row * a.ldr + col;
+    if (ncols_valid >= 32) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        uint4 q = *reinterpret_cast<const uint4*>(r + i);
+        float2 f0 = unpack_bf16x2(q.x), f1 = unpack_bf16x2(q.y), f2 = unpack_bf16x2(q.z), f3 = unpack_bf16x2(q.w);
+        v[i] += f0.x; v[i + 1] += f0.y; v[i + 2] += f1.x; v[i + 3] += f1.y;
+        v[i + 4] += f2.x; v[i + 5] += f2.y; v[i + 6] += f3.x; v[i + 7] += f3.y;
+      }
+    } else {
+      for (int i = 0; i < ncols_valid; ++i) v[i] += __bfloat162float(r[i]);
+    }
+  }
+  if (ncols_valid >= 32) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+      uint4 o;
+      o.x = pack_bf16x2(v[i], v[i + 1]);
+      o.y = pack_bf16x2(v[i + 2], v[i + 3]);
+      o.z = pack_bf16x2(v[i + 4], v[i + 5]);
+      o.w = pack_bf16x2(v[i + 6], v[i + 7]);
+      *reinterpret_cast<uint4*>(p + i) = o;
+    }
+  } else {
+    for (int i = 0; i < ncols_valid; ++i) p[i] = __float2bfloat16_rn(v[i]);
+  }
+}
+
+__device__ __forceinline__ void store_bf16_32(__nv_bfloat16* p, const float (&v)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    uint4 o;
+    o.x = pack_bf16x2(v[i], v[i + 1]);
+    o.y = pack_bf16x2(v[i + 2], v[i + 3]);
+    o.z = pack_bf16x2(v[i + 4], v[i + 5]);
+    o.w = pack_bf16x2(v[i + 6], v[i + 7]);
+    *reinterpret_cast<uint4*>(p + i) = o;
+  }
+}
+
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase, int mb, int nb, int quad,
+                                              int lane) {
+  const int row = mb * BM + quad * 32 + lane;
+  const bool row_ok = row < a.M;
+  const uint32_t trow = tbase + ((uint32_t)(quad * 32) << 16);
+  if (EPI == EPI_SWIGLU) {
+    // TMEM columns [0,128): gate, [128,256): up, for output columns nb*128 + [0,128)
+    const int c0 = nb * 128;
+#pragma unroll 1
+    for (int c = 0; c < 128; c += 32) {
+      float g[32], u[32];
+      tmem_ld32(trow + c, g);
+      tmem_ld32(trow + 128 + c, u);
+      if (row_ok) {
+        __nv_bfloat16* gp = a.D2 + (long)row * a.ldd2 + c0 + c;
+        __nv_bfloat16* up = gp + a.ffn;
+        // the backward recomputes from the rounded g/u, so round first
+        float gr[32], ur[32], h[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          gr[i] = __bfloat162float(__float2bfloat16_rn(g[i]));
+          ur[i] = __bfloat162float(__float2bfloat16_rn(u[i]));
+          h[i] = gr[i] / (1.f + __expf(-gr[i])) * ur[i];
+        }
+        store_bf16_32(gp, gr);
+        store_bf16_32(up, ur);
+        store_bf16_32(reinterpret_cast<__nv_bfloat16*>(a.D) + (long)row * a.ldd + c0 + c, h);
+      }
+    }
+    return;
+  }
+  const int n0 = nb * BN;
+  if (EPI == EPI_ROPE) {
+    const int hd = a.head_dim, half = hd >> 1;
+    const int pos = row % a.seqlen;
+#pragma unroll 1
+    for (int h0 = 0; h0 < BN; h0 += hd) {
+      const int col = n0 + h0;
+      if (col >= a.N) break;
+      if (col < a.rope_cols) {
+#pragma unroll 1
+        for (int j = 0; j < half; j += 32) {
+          float x1[32], x2[32];
+          tmem_ld32(trow + h0 + j, x1);
+          tmem_ld32(trow + h0 + half + j, x2);
+          if (row_ok) {
+            const float* cs = a.cos_t + (long)pos * hd + j;
+            const float* sn = a.sin_t + (long)pos * hd + j;
+            float y1[32], y2[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float c = cs[i], s = sn[i];
+              y1[i] = x1[i] * c - x2[i] * s;
+              y2[i] = x2[i] * c + x1[i] * s;
+            }
+            __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(a.D) + (long)row * a.ldd + col + j;
+            store_bf16_32(p, y1);
+            store_bf16_32(p + half, y2);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int j = 0; j < hd; j += 32) {
+          float x[32];
+          tmem_ld32(trow + h0 + j, x);
+          if (row_ok) store_chunk<EPI_STORE_BF16>(a, row, col + j, x, 32);
+        }
+      }
+    }
+    return;
+  }
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    if (n0 + c >= a.N) break;
+    float v[32];
+    tmem_ld32(trow + c, v);
+    if (row_ok) store_chunk<EPI>(a, row, n0 + c, v, min(32, a.N - (n0 + c)));
+  }
+}
+
+// ---------------------------------------------------------------- kernel
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const GemmArgs args) {
+  using L = SmemLayout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  constexpr uint32_t IDESC = idesc_bf16(BM, BN, A_MN, B_MN);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_phase[STAGES];
+      bool issued[STAGES];
+      for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_phase[s] = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, args.m_blocks, args.n_blocks, mb, nb);
+        for (int k = 0; k < args.k_iters; ++k) {
+          if (*abort_flag || !mbar_wait(&empty[stage], phase ^ 1, args.err)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * L::STAGE_BYTES;
+          uint8_t* sb = sa + L::A_BYTES;
+          mbar_arrive_expect_tx(&full[stage], L::STAGE_BYTES);
+          if (!A_MN) {
+            tma_load_2d(sa, &tmA, &full[stage], k * BK, mb * BM);
+          } else {
+            tma_load_2d(sa, &tmA, &full[stage], mb * BM, k * BK);
+            tma_load_2d(sa + 8192, &tmA, &full[stage], mb * BM + 64, k * BK);
+          }
+          if (!B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j) {
+              int r = (EPI == EPI_SWIGLU) ? (j == 0 ? nb * 128 : args.ffn + nb * 128) : nb * BN + j * 128;
+              tma_load_2d(sb + j * 16384, &tmB, &full[stage], k * BK, r);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 8192, &tmB, &full[stage], nb * BN + j * 64, k * BK);
+          }
+          issued[stage] = true;
+          issued_phase[stage] = phase;
+          if (++stage == STAGES) stage = 0, phase ^= 1;
+        }
+      }
+      if (!ok) {
+        // drain copies still in flight before the CTA's shared memory goes away
+        for (int s = 0; s < STAGES; ++s)
+          if (issued[s]) mbar_wait(&full[s], issued_phase[s], args.err);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int t = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x, ++t) {
+        const int acc = t & 1;
+        const uint32_t acc_phase = (t >> 1) & 1;
+        if (*abort_flag || !mbar_wait(&acc_empty[acc], acc_phase ^ 1, args.err)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * BN;
+        for (int k = 0; k < args.k_iters; ++k) {
+          if (*abort_flag || !mbar_wait(&full[stage], phase, args.err)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + stage * L::STAGE_BYTES);
+          const uint32_t b0 = a0 + L::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? sdesc_sw128(a0 + kk * 2048, 8192, 1024) : sdesc_sw128(a0 + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(b0 + kk * 2048, 8192, 1024) : sdesc_sw128(b0 + kk * 32, 16, 1024);
+            umma_bf16(d, ad, bd, IDESC, (k | kk) != 0);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) stage = 0, phase ^= 1;
+        }
+        umma_commit(&acc_full[acc]);
+      }
+    }
+  } else {
+    const int quad = warp & 3;
+    int t = 0;
+    for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++t) {
+      const int acc = t & 1;
+      const uint32_t acc_phase = (t >> 1) & 1;
+      int mb, nb;
+      tile_coords(tile, args.m_blocks, args.n_blocks, mb, nb);
+      if (*abort_flag || !mbar_wait(&acc_full[acc], acc_phase, args.err)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      epilogue_tile<BN, EPI>(args, tmem_base + acc * BN, mb, nb, quad, lane);
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, 2 * BN);
+}
+
+// ---------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    C10_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && p, "cuTensorMapEncodeTiled not available");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, inner] matrix, box [box_rows, 64].
+static CUtensorMap make_map(const void* base, long inner, long rows, long row_stride_elems, int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_stride_elems * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with ", (int)r);
+  return m;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    C10_CUDA_CHECK(cudaGetDevice(&dev));
+    C10_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+  }
+  return n;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+static void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t st) {
+  using L = SmemLayout<BN, STAGES>;
+  auto kern = gemm_tcgen05_kernel<BN, STAGES, A_MN, B_MN, EPI>;
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    configured = true;
+  }
+  const int grid = std::min(g.num_tiles, num_sms());
+  if (grid == 0) return;
+  kern<<<grid, 192, L::TOTAL, st>>>(ta, tb, g);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+template <int BN, bool A_MN, bool B_MN>
+static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t st) {
+  constexpr int ST = BN == 256 ? 4 : 6;
+  switch (epi) {
+    case EPI_STORE_BF16: launch<BN, ST, A_MN, B_MN, EPI_STORE_BF16>(ta, tb, g, st); break;
+    case EPI_STORE_F32: launch<BN, ST, A_MN, B_MN, EPI_STORE_F32>(ta, tb, g, st); break;
+    case EPI_ACC_F32: launch<BN, ST, A_MN, B_MN, EPI_ACC_F32>(ta, tb, g, st); break;
+    case EPI_RESIDUAL:
+      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_RESIDUAL>(ta, tb, g, st); break; }
+      TORCH_CHECK(false, "residual epilogue needs K-major operands");
+    case EPI_ROPE:
+      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_ROPE>(ta, tb, g, st); break; }
+      TORCH_CHECK(false, "rope epilogue needs K-major operands");
+    case EPI_SWIGLU:
+      if constexpr (!A_MN && !B_MN && BN == 256) { launch<BN, ST, A_MN, B_MN, EPI_SWIGLU>(ta, tb, g, st); break; }
+      TORCH_CHECK(false, "swiglu epilogue needs K-major operands and BN=256");
+    default: TORCH_CHECK(false, "unknown epilogue ", epi);
+  }
+}
+
+}  // namespace dtb
+
+// Python entry: see ops/gemm.py for the operand conventions.
+//   A: [M,K] (a_mn=false) or [K,M] (a_mn=true); B: [N,K] or [K,N]; D: [M,N]
+//   (SwiGLU: B = [2F,K], D = [M,F], D2 = [M,2F]; p0 = F).
+void gemm_entry(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_mn, bool b_mn, int64_t epi,
+                c10::optional<torch::Tensor> R, c10::optional<torch::Tensor> alpha,
+                c10::optional<torch::Tensor> cos_t, c10::optional<torch::Tensor> sin_t,
+                c10::optional<torch::Tensor> D2, int64_t p0, int64_t p1) {
+  using namespace dtb;
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && D.is_cuda(), "gemm: CUDA tensors expected");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm: bf16 operands expected");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.is_contiguous() && B.is_contiguous(), "gemm: 2-D contiguous operands");
+  const c10::cuda::CUDAGuard guard(A.device());
+  const long M = a_mn ? A.size(1) : A.size(0);
+  const long K = a_mn ? A.size(0) : A.size(1);
+  const long Kb = b_mn ? B.size(0) : B.size(1);
+  long NB = b_mn ? B.size(1) : B.size(0);
+  TORCH_CHECK(K == Kb, "gemm: reduction sizes differ (", K, " vs ", Kb, ")");
+  TORCH_CHECK(A.size(1) % 8 == 0 && B.size(1) % 8 == 0, "gemm: row strides must be multiples of 16 bytes");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(A.data_ptr()) & 15) == 0 && (reinterpret_cast<uintptr_t>(B.data_ptr()) & 15) == 0,
+              "gemm: operands must be 16-byte aligned");
+  GemmArgs g{};
+  g.M = (int)M;
+  g.K = (int)K;
+  g.D = D.data_ptr();
+  g.ldd = D.stride(0);
+  g.err = dtb_error_word();
+  const bool f32out = D.scalar_type() == at::kFloat;
+  int e = (int)epi;
+  if (e == EPI_STORE_BF16 && f32out) e = EPI_STORE_F32;
+  if (e == EPI_ACC_F32) TORCH_CHECK(f32out, "gemm: accumulate epilogue needs an fp32 output");
+  if (e == EPI_STORE_BF16 || e == EPI_RESIDUAL || e == EPI_ROPE || e == EPI_SWIGLU)
+    TORCH_CHECK(D.scalar_type() == at::kBFloat16, "gemm: bf16 output expected");
+  TORCH_CHECK(D.stride(1) == 1 && D.stride(0) % 8 == 0, "gemm: output rows must be contiguous and 16B aligned");
+  if (alpha.has_value()) {
+    TORCH_CHECK(alpha->scalar_type() == at::kFloat && alpha->is_cuda(), "gemm: alpha must be a CUDA fp32 scalar");
+    g.alpha = alpha->data_ptr<float>();
+  }
+  int BN = NB > 128 ? 256 : 128;
+  if (e == EPI_RESIDUAL) {
+    TORCH_CHECK(R.has_value() && R->scalar_type() == at::kBFloat16 && R->stride(1) == 1, "gemm: bad residual");
+    g.R = reinterpret_cast<const __nv_bfloat16*>(R->data_ptr());
+    g.ldr = R->stride(0);
+  }
+  if (e == EPI_ROPE) {
+    g.rope_cols = (int)p0;
+    g.head_dim = (int)(p1 >> 16);
+    g.seqlen = (int)(p1 & 0xFFFF);
+    TORCH_CHECK(g.head_dim % 64 == 0 && BN % g.head_dim == 0, "gemm: rope epilogue needs head_dim in {64,128,256}");
+    TORCH_CHECK(cos_t.has_value() && sin_t.has_value(), "gemm: rope tables missing");
+    g.cos_t = cos_t->data_ptr<float>();
+    g.sin_t = sin_t->data_ptr<float>();
+  }
+  if (e == EPI_SWIGLU) {
+    TORCH_CHECK(D2.has_value(), "gemm: swiglu needs D2");
+    g.ffn = (int)p0;
+    TORCH_CHECK(g.ffn % 128 == 0 && NB == 2 * g.ffn, "gemm: swiglu needs B=[2F,K] with F % 128 == 0");
+    g.D2 = reinterpret_cast<__nv_bfloat16*>(D2->data_ptr());
+    g.ldd2 = D2->stride(0);
+    BN = 256;
+    g.N = g.ffn;
+    g.n_blocks = g.ffn / 128;
+  } else {
+    g.N = (int)NB;
+    g.n_blocks = (int)((NB + BN - 1) / BN);
+  }
+  g.m_blocks = (int)((M + BM - 1) / BM);
+  g.k_iters = (int)((K + BK - 1) / BK);
+  g.num_tiles = g.m_blocks * g.n_blocks;
+  TORCH_CHECK(D.size(0) == M && D.size(1) == g.N, "gemm: output shape mismatch");
+  // tensor maps: A box = 128 rows (K-major) or 64 K-rows (MN-major); B likewise
+  const CUtensorMap ta = a_mn ? make_map(A.data_ptr(), M, K, A.stride(0), BK) : make_map(A.data_ptr(), K, M, A.stride(0), BM);
+  const CUtensorMap tb = b_mn ? make_map(B.data_ptr(), NB, K, B.stride(0), BK) : make_map(B.data_ptr(), K, NB, B.stride(0), 128);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (BN == 256) {
+    if (!a_mn && !b_mn) dispatch_epi<256, false, false>(e, ta, tb, g, st);
+    else if (!a_mn && b_mn) dispatch_epi<256, false, true>(e, ta, tb, g, st);
+    else if (a_mn && b_mn) dispatch_epi<256, true, true>(e, ta, tb, g, st);
+    else TORCH_CHECK(false, "gemm: layout (MN, K) not built");
+  } else {
+    if (!a_mn && !b_mn) dispatch_epi<128, false, false>(e, ta, tb, g, st);
+    else if (!a_mn && b_mn) dispatch_epi<128, false, true>(e, ta, tb, g, st);
+    else if (a_mn && b_mn) dispatch_epi<128, true, true>(e, ta, tb, g, st);
+    else TORCH_CHECK(false, "gemm: layout (MN, K) not built");
+  }
+}

@@ -1,0 +1,248 @@
+"""Numerics of every sm_100a kernel against a plain PyTorch fp32 restatement of the op."""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():  # pragma: no cover - collected on CPU boxes, skipped by marker
+    pytest.skip("needs a GPU", allow_module_level=True)
+
+from build_your_own_distributed_training_b200.ops import gemm  # noqa: E402
+from build_your_own_distributed_training_b200.ops._ext import native  # noqa: E402
+
+DEV = torch.device("cuda", 0)
+BF = torch.bfloat16
+
+
+def _rel(a: torch.Tensor, b: torch.Tensor) -> float:
+    a, b = a.float(), b.float()
+    return float((a - b).norm() / b.norm().clamp_min(1e-12))
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    yield
+    assert native().device_error() == 0
+
+
+def _rand(*shape, scale=1.0):
+    return (torch.randn(*shape, device=DEV) * scale).to(BF)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 1024), (200, 384, 136), (4096, 4096, 4096),
+                                   (1000, 96, 512), (64, 32000, 256)])
+def test_gemm_nt(M, N, K):
+    a, b = _rand(M, K), _rand(N, K)
+    ref = a.float() @ b.float().t()
+    out = gemm.mm_nt(a, b)
+    assert out.dtype == BF
+    assert _rel(out, ref) < 1e-2
+    out32 = gemm.mm_nt(a, b, out_dtype=torch.float32)
+    assert _rel(out32, ref) < 1e-5
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (512, 768, 256), (4096, 4096, 11008), (136, 200, 320)])
+def test_gemm_nn(M, N, K):
+    a, b = _rand(M, K), _rand(K, N)
+    ref = a.float() @ b.float()
+    assert _rel(gemm.mm_nn(a, b), ref) < 1e-2
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (768, 256, 512), (4096, 4096, 4096), (200, 136, 96)])
+def test_gemm_tn_accumulate(M, N, K):
+    a, b = _rand(K, M), _rand(K, N)
+    acc = torch.randn(M, N, device=DEV)
+    ref = acc + a.float().t() @ b.float()
+    gemm.mm_tn_acc(a, b, acc)
+    assert _rel(acc, ref) < 1e-5
+
+
+def test_gemm_alpha_and_residual():
+    a, b, r = _rand(256, 512), _rand(384, 512), _rand(256, 384)
+    alpha = torch.tensor([0.25], device=DEV)
+    ref = 0.25 * (a.float() @ b.float().t()) + r.float()
+    # alpha applies before the residual add
+    out = torch.empty(256, 384, device=DEV, dtype=BF)
+    native().gemm(a, b, out, False, False, gemm.EPI_RESIDUAL, r, alpha, None, None, None, 0, 0)
+    assert _rel(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("hd,nq,nkv", [(128, 4, 4), (64, 8, 2)])
+def test_gemm_rope_epilogue(hd, nq, nkv):
+    from build_your_own_distributed_training_b200.ops.rope import precompute_rope_cache, rope_forward
+    seqlen, b, d = 256, 2, 512
+    x, w = _rand(b * seqlen, d), _rand((nq + 2 * nkv) * hd, d, scale=0.05)
+    cos, sin = precompute_rope_cache(hd, 512, 10000.0, DEV)
+    rope_cols = (nq + nkv) * hd
+    out = gemm.mm_nt_rope(x, w, cos, sin, rope_cols, hd, seqlen)
+    ref = x.float() @ w.float().t()
+    rope_forward(ref, cos, sin, rope_cols, hd, seqlen)
+    assert _rel(out, ref) < 1e-2
+
+
+def test_gemm_swiglu_epilogue():
+    M, K, Fh = 512, 256, 384
+    x, w = _rand(M, K), _rand(2 * Fh, K, scale=0.1)
+    act, gu = gemm.mm_nt_swiglu(x, w, Fh)
+    ref_gu = x.float() @ w.float().t()
+    ref = F.silu(ref_gu[:, :Fh]) * ref_gu[:, Fh:]
+    assert _rel(gu, ref_gu) < 1e-2
+    assert _rel(act, ref) < 2e-2
+
+
+def test_rmsnorm_fwd_bwd():
+    from build_your_own_distributed_training_b200.ops.norm import rms_norm
+    x = _rand(1000, 4096).requires_grad_()
+    w = (1 + 0.1 * torch.randn(4096, device=DEV)).to(BF).requires_grad_()
+    y = rms_norm(x, w, 1e-5)
+    xr = x.detach().float().requires_grad_()
+    wr = w.detach().float().requires_grad_()
+    yr = xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-5) * wr
+    assert _rel(y, yr) < 1e-2
+    g = torch.randn_like(yr)
+    y.backward(g.to(BF))
+    yr.backward(g)
+    assert _rel(x.grad, xr.grad) < 2e-2
+    assert _rel(w.grad, wr.grad) < 2e-2
+
+
+def test_rmsnorm_backward_is_deterministic():
+    from build_your_own_distributed_training_b200.ops.norm import _RMSNormFn
+    x = _rand(4096, 4096)
+    w = torch.ones(4096, device=DEV, dtype=BF)
+    dy = _rand(4096, 4096)
+    outs = []
+    for _ in range(3):
+        acc = torch.zeros(4096, device=DEV)
+        _, rstd = native().rmsnorm_fwd(x, w, 1e-5)
+        dx = native().rmsnorm_bwd(dy, x, w, rstd, acc)
+        outs.append((dx, acc))
+    for dx, acc in outs[1:]:
+        assert torch.equal(dx, outs[0][0]) and torch.equal(acc, outs[0][1])
+    del _RMSNormFn
+
+
+def test_rope_bwd_is_transpose():
+    from build_your_own_distributed_training_b200.ops.rope import precompute_rope_cache, rope_backward_, rope_forward
+    hd, seqlen = 128, 128
+    cos, sin = precompute_rope_cache(hd, 256, 10000.0, DEV)
+    d = _rand(2 * seqlen, 6 * hd)
+    ref = d.float().cpu().clone()
+    rope_backward_(ref, cos.cpu(), sin.cpu(), 4 * hd, hd, seqlen)
+    out = d.clone()
+    rope_backward_(out, cos, sin, 4 * hd, hd, seqlen)
+    assert _rel(out.cpu(), ref) < 1e-2
+    # forward then backward is the identity (rotation is orthogonal)
+    y = d.float().cpu()
+    rope_forward(y, cos.cpu(), sin.cpu(), 4 * hd, hd, seqlen)
+    rope_backward_(y, cos.cpu(), sin.cpu(), 4 * hd, hd, seqlen)
+    assert _rel(y, d.float().cpu()) < 1e-5
+
+
+def test_swiglu_bwd():
+    from build_your_own_distributed_training_b200.ops.linear import swiglu_backward
+    M, Fh = 300, 256
+    gu, da = _rand(M, 2 * Fh), _rand(M, Fh)
+    out = swiglu_backward(da, gu, Fh)
+    ref = swiglu_backward(da.cpu().float(), gu.cpu().float(), Fh)
+    assert _rel(out.cpu(), ref) < 1e-2
+
+
+def test_embedding_fwd_bwd_deterministic():
+    V, D, M = 1000, 256, 4096
+    w = _rand(V, D)
+    tok = torch.randint(0, V, (M,), device=DEV)
+    out = native().embedding_fwd(tok, w, BF)
+    assert torch.equal(out, w[tok])
+    dout = _rand(M, D)
+    accs = []
+    for _ in range(2):
+        acc = torch.zeros(V, D, device=DEV)
+        native().embedding_bwd(tok, dout, acc)
+        accs.append(acc)
+    ref = torch.zeros(V, D, device=DEV).index_add_(0, tok, dout.float())
+    assert _rel(accs[0], ref) < 1e-5
+    assert torch.equal(accs[0], accs[1])
+
+
+@pytest.mark.parametrize("M,V", [(512, 32000), (100, 1000)])
+def test_cross_entropy(M, V):
+    logits = torch.randn(M, V, device=DEV) * 3
+    labels = torch.randint(0, V, (M,), device=DEV)
+    labels[::7] = -100
+    loss, dlog = native().cross_entropy_fwd(logits, labels, -100)
+    lr = logits.clone().requires_grad_()
+    ref = F.cross_entropy(lr, labels, ignore_index=-100)
+    ref.backward()
+    assert abs(float(loss) - float(ref)) < 1e-4 * max(1.0, float(ref))
+    assert _rel(dlog, lr.grad) < 1e-2
+
+
+def test_adamw_matches_torch():
+    n = 100_003
+    p = torch.randn(n, device=DEV)
+    g = torch.randn(n, device=DEV)
+    m, v = torch.zeros(n, device=DEV), torch.zeros(n, device=DEV)
+    out = torch.empty(n, device=DEV, dtype=BF)
+    ref = p.clone().requires_grad_()
+    opt = torch.optim.AdamW([ref], lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    clip = torch.tensor([0.5, 1.0], device=DEV)
+    for step in range(1, 4):
+        ref.grad = g * 0.5
+        opt.step()
+        native().adamw(p, g, m, v, out, clip, 1e-3, 0.9, 0.95, 1e-8, 0.1, step)
+    assert _rel(p, ref.detach()) < 1e-6
+    assert torch.equal(out, p.to(BF))
+    # non-finite flag skips the update
+    before = p.clone()
+    native().adamw(p, g, m, v, out, torch.tensor([0.0, 0.0], device=DEV), 1e-3, 0.9, 0.95, 1e-8, 0.1, 4)
+    assert torch.equal(p, before)
+
+
+def test_sumsq():
+    x = torch.randn(10_000_019, device=DEV)
+    s = native().sumsq(x)
+    assert abs(float(s) - float(x.double().pow(2).sum())) / float(x.double().pow(2).sum()) < 1e-5
+    assert torch.equal(s, native().sumsq(x))
+
+
+def _attn_ref(qkv, b, s, nq, nkv, hd):
+    from build_your_own_distributed_training_b200.ops.attention import attention_reference
+    return attention_reference(qkv.float(), b, s, nq, nkv, hd)
+
+
+@pytest.mark.parametrize("b,s,nq,nkv,hd", [(2, 128, 4, 4, 128), (1, 256, 8, 2, 64), (2, 192, 4, 1, 128),
+                                           (1, 1024, 2, 2, 128)])
+def test_attention_fwd_bwd(b, s, nq, nkv, hd):
+    from build_your_own_distributed_training_b200.ops.attention import causal_attention
+    qkv = _rand(b * s, (nq + 2 * nkv) * hd).requires_grad_()
+    o = causal_attention(qkv, b, s, nq, nkv, hd)
+    ref_in = qkv.detach().float().requires_grad_()
+    ref = _attn_ref(ref_in, b, s, nq, nkv, hd)
+    assert _rel(o, ref) < 2e-2
+    do = torch.randn_like(ref)
+    o.backward(do.to(BF))
+    ref.backward(do)
+    assert _rel(qkv.grad, ref_in.grad) < 3e-2
+    # bit-reproducible backward
+    g1 = qkv.grad.clone()
+    qkv.grad = None
+    causal_attention(qkv, b, s, nq, nkv, hd).backward(do.to(BF))
+    assert torch.equal(qkv.grad, g1)
+
+
+def test_attention_lse_scale():
+    b, s, nq, nkv, hd = 1, 128, 2, 2, 64
+    qkv = _rand(b * s, (nq + 2 * nkv) * hd)
+    o, lse = native().attn_fwd(qkv, b, s, nq, nkv, hd, 1 / math.sqrt(hd))
+    q = qkv.float()[:, :nq * hd].view(s, nq, hd).transpose(0, 1)
+    k = qkv.float()[:, nq * hd:(nq + nkv) * hd].view(s, nkv, hd).transpose(0, 1)
+    sc = q @ k.transpose(1, 2) / math.sqrt(hd)
+    sc = sc.masked_fill(torch.triu(torch.ones(s, s, device=DEV, dtype=torch.bool), 1), float("-inf"))
+    assert _rel(lse[0], torch.logsumexp(sc, -1)) < 1e-4
