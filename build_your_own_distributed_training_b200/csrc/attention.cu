@@ -513,7 +513,7 @@ void fwd_launch(const __nv_bfloat16* qkv, __nv_bfloat16* o, float* lse, int B, i
   const int smem = (64 + 4 * 64) * HD * 2;
   static bool cfg = false;
   if (!cfg) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    DTB_CUDA(cudaFuncSetAttribute(attn_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     cfg = true;
   }
   dim3 grid(S / 64, nq, B);
@@ -530,8 +530,8 @@ void bwd_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* o, const __nv_bfl
   const int smem_q = (2 * 64 + 4 * 32) * HD * 2;
   static bool cfg = false;
   if (!cfg) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dkdv_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv));
-    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q));
+    DTB_CUDA(cudaFuncSetAttribute(attn_bwd_dkdv_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv));
+    DTB_CUDA(cudaFuncSetAttribute(attn_bwd_dq_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q));
     cfg = true;
   }
   attn_bwd_dkdv_kernel<HD><<<dim3(S / 64, nkv, B), 128, smem_kv, st>>>(qkv, dO, lse, Dv, dqkv, S, nq, nkv, scale,
@@ -564,7 +564,7 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t B, int64_t S, int
   auto op = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
   if (hd == 128) attn::fwd_launch<128>(q, op, lse.data_ptr<float>(), B, S, nq, nkv, (float)scale, st);
   else attn::fwd_launch<64>(q, op, lse.data_ptr<float>(), B, S, nq, nkv, (float)scale, st);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  DTB_LAUNCH_CHECK();
   return {o, lse};
 }
 
@@ -584,6 +584,6 @@ torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qkv, torch::Tensor o, tor
   else
     attn::bwd_launch<64>(cast(qkv), cast(o), cast(dO), lse.data_ptr<float>(), Dv.data_ptr<float>(), dq, B, S, nq, nkv,
                          (float)scale, st);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  DTB_LAUNCH_CHECK();
   return dqkv;
 }

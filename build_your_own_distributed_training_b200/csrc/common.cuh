@@ -183,6 +183,27 @@ __device__ __forceinline__ float warp_max(float v) {
 
 }  // namespace dtb
 
+// Host-side argument/CUDA checks that format with snprintf (no iostreams),
+// print the message to stderr and throw std::runtime_error (RuntimeError in
+// Python).
+#include <cstdio>
+#include <stdexcept>
+#define DTB_CHECK(cond, ...)                                                       \
+  do {                                                                             \
+    if (!(cond)) {                                                                 \
+      char dtb_msg_[512];                                                          \
+      std::snprintf(dtb_msg_, sizeof(dtb_msg_), __VA_ARGS__);                     \
+      std::fprintf(stderr, "[dtb] check failed at %s:%d: %s\n", __FILE__, __LINE__, dtb_msg_); \
+      throw std::runtime_error(dtb_msg_);                                          \
+    }                                                                              \
+  } while (0)
+#define DTB_CUDA(call)                                                             \
+  do {                                                                             \
+    cudaError_t dtb_e_ = (call);                                                   \
+    DTB_CHECK(dtb_e_ == cudaSuccess, "%s failed: %s", #call, cudaGetErrorString(dtb_e_)); \
+  } while (0)
+#define DTB_LAUNCH_CHECK() DTB_CUDA(cudaGetLastError())
+
 // Host side: the per-device error word kernels write to (allocated once per
 // device by the runtime, see runtime.cpp).
 int* dtb_error_word();

@@ -354,7 +354,7 @@ std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double 
     rmsnorm_fwd_kernel<__nv_bfloat16, 256><<<M, 256, 0, cur_stream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
         reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), rstd.data_ptr<float>(), D, (float)eps);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  DTB_LAUNCH_CHECK();
   return {y, rstd};
 }
 
@@ -393,7 +393,7 @@ torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, to
                      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), w.data_ptr(), w.scalar_type() == at::kFloat,
                      rstd.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), dw_acc.data_ptr<float>(),
                      part.data_ptr<float>(), M, D, rpc, cur_stream());
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  DTB_LAUNCH_CHECK();
   return dx;
 }
 
@@ -407,7 +407,7 @@ void rope_apply(torch::Tensor x, torch::Tensor cos_t, torch::Tensor sin_t, int64
   rope_kernel<<<grid_for(total, 256), 256, 0, cur_stream()>>>(
       reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), x.stride(0), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), M,
       (int)rope_cols, (int)hd, (int)seqlen, (float)sign);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  DTB_LAUNCH_CHECK();
 }
 
 void rope_bwd(torch::Tensor d, torch::Tensor c, torch::Tensor s, int64_t rc, int64_t hd, int64_t sl) {
@@ -426,7 +426,7 @@ void swiglu_bwd(torch::Tensor da, torch::Tensor gu, torch::Tensor dgu) {
   swiglu_bwd_kernel<<<grid_for(total, 256), 256, 0, cur_stream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(da.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()), M, F);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  DTB_LAUNCH_CHECK();
 }
 
 torch::Tensor embedding_fwd(torch::Tensor tok, torch::Tensor w, c10::ScalarType out_dtype) {
@@ -450,7 +450,7 @@ torch::Tensor embedding_fwd(torch::Tensor tok, torch::Tensor w, c10::ScalarType 
     embedding_fwd_kernel<__nv_bfloat16, __nv_bfloat16><<<M, nt, 0, st>>>(
         tok.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
         reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), D, V, err);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  DTB_LAUNCH_CHECK();
   return out;
 }
 
@@ -466,7 +466,7 @@ void embedding_bwd(torch::Tensor tok, torch::Tensor dout, torch::Tensor acc) {
   embedding_bwd_kernel<<<M, std::min(256, std::max(32, D)), 0, cur_stream()>>>(
       st_tok.data_ptr<int64_t>(), order.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
       acc.data_ptr<float>(), M, D, V);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  DTB_LAUNCH_CHECK();
 }
 
 std::vector<torch::Tensor> cross_entropy_fwd(torch::Tensor logits, torch::Tensor labels, int64_t ignore) {
@@ -485,7 +485,7 @@ std::vector<torch::Tensor> cross_entropy_fwd(torch::Tensor logits, torch::Tensor
                                          reinterpret_cast<__nv_bfloat16*>(dlog.data_ptr()), rows.data_ptr<float>(),
                                          nvalid.data_ptr<int>(), V, ignore);
   ce_finish_kernel<1024><<<1, 1024, 0, st>>>(rows.data_ptr<float>(), nvalid.data_ptr<int>(), loss.data_ptr<float>(), M);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  DTB_LAUNCH_CHECK();
   return {loss, dlog};
 }
 
@@ -502,7 +502,7 @@ void adamw(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, t
       p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), clip.has_value() ? clip->data_ptr<float>() : nullptr, n,
       (float)lr, (float)b1, (float)b2, (float)eps, (float)wd, bc1, bc2s);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  DTB_LAUNCH_CHECK();
 }
 
 torch::Tensor sumsq(torch::Tensor x) {
@@ -515,6 +515,6 @@ torch::Tensor sumsq(torch::Tensor x) {
   auto st = cur_stream();
   sumsq_part_kernel<256><<<nb, 256, 0, st>>>(x.data_ptr<float>(), n, part.data_ptr<float>());
   sum_parts_kernel<1024><<<1, 1024, 0, st>>>(part.data_ptr<float>(), nb, out.data_ptr<float>());
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  DTB_LAUNCH_CHECK();
   return out;
 }

@@ -32,6 +32,8 @@
 
 #include "common.cuh"
 
+bool dtb_debug_enabled();
+
 namespace dtb {
 
 enum Epi : int {
@@ -387,15 +389,27 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   if (!fn) {
     cudaDriverEntryPointQueryResult q;
     void* p = nullptr;
-    C10_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
-    TORCH_CHECK(q == cudaDriverEntryPointSuccess && p, "cuTensorMapEncodeTiled not available");
+    DTB_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    DTB_CHECK(q == cudaDriverEntryPointSuccess && p, "cuTensorMapEncodeTiled not available");
     fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
   }
   return fn;
 }
 
+// cuTensorMapEncodeTiled is a driver-API call and needs a current context on
+// the calling thread; autograd's worker threads may not have bound one yet
+// (the runtime binds the primary context lazily), so do it once per thread.
+static void bind_context_once() {
+  static thread_local bool bound = false;
+  if (!bound) {
+    DTB_CUDA(cudaFree(nullptr));
+    bound = true;
+  }
+}
+
 // 2-D bf16 tensor map over a row-major [rows, inner] matrix, box [box_rows, 64].
 static CUtensorMap make_map(const void* base, long inner, long rows, long row_stride_elems, int box_rows) {
+  bind_context_once();
   CUtensorMap m;
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)row_stride_elems * 2};
@@ -404,7 +418,7 @@ static CUtensorMap make_map(const void* base, long inner, long rows, long row_st
   CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with ", (int)r);
+  DTB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (%d): inner=%ld rows=%ld stride=%ld box_rows=%d base=%p", (int)r, inner, rows, row_stride_elems, box_rows, base);
   return m;
 }
 
@@ -412,8 +426,8 @@ static int num_sms() {
   static int n = 0;
   if (!n) {
     int dev;
-    C10_CUDA_CHECK(cudaGetDevice(&dev));
-    C10_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    DTB_CUDA(cudaGetDevice(&dev));
+    DTB_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
   }
   return n;
 }
@@ -424,13 +438,13 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cu
   auto kern = gemm_tcgen05_kernel<BN, STAGES, A_MN, B_MN, EPI>;
   static bool configured = false;
   if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    DTB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
     configured = true;
   }
   const int grid = std::min(g.num_tiles, num_sms());
   if (grid == 0) return;
   kern<<<grid, 192, L::TOTAL, st>>>(ta, tb, g);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  DTB_LAUNCH_CHECK();
 }
 
 template <int BN, bool A_MN, bool B_MN>
@@ -449,7 +463,7 @@ static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, 
     case EPI_SWIGLU:
       if constexpr (!A_MN && !B_MN && BN == 256) { launch<BN, ST, A_MN, B_MN, EPI_SWIGLU>(ta, tb, g, st); break; }
       TORCH_CHECK(false, "swiglu epilogue needs K-major operands and BN=256");
-    default: TORCH_CHECK(false, "unknown epilogue ", epi);
+    default: DTB_CHECK(false, "unknown epilogue %d", epi);
   }
 }
 
@@ -471,7 +485,7 @@ void gemm_entry(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_mn, bo
   const long K = a_mn ? A.size(0) : A.size(1);
   const long Kb = b_mn ? B.size(0) : B.size(1);
   long NB = b_mn ? B.size(1) : B.size(0);
-  TORCH_CHECK(K == Kb, "gemm: reduction sizes differ (", K, " vs ", Kb, ")");
+  DTB_CHECK(K == Kb, "gemm: reduction sizes differ (%ld vs %ld)", K, Kb);
   TORCH_CHECK(A.size(1) % 8 == 0 && B.size(1) % 8 == 0, "gemm: row strides must be multiples of 16 bytes");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(A.data_ptr()) & 15) == 0 && (reinterpret_cast<uintptr_t>(B.data_ptr()) & 15) == 0,
               "gemm: operands must be 16-byte aligned");
@@ -525,6 +539,9 @@ void gemm_entry(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_mn, bo
   g.num_tiles = g.m_blocks * g.n_blocks;
   TORCH_CHECK(D.size(0) == M && D.size(1) == g.N, "gemm: output shape mismatch");
   // tensor maps: A box = 128 rows (K-major) or 64 K-rows (MN-major); B likewise
+  if (dtb_debug_enabled())
+    fprintf(stderr, "[dtb] gemm M=%ld N=%d K=%ld a_mn=%d b_mn=%d epi=%d BN=%d A=%p B=%p D=%p alpha=%p\n", M, g.N, K,
+            (int)a_mn, (int)b_mn, e, BN, A.data_ptr(), B.data_ptr(), D.data_ptr(), (const void*)g.alpha);
   const CUtensorMap ta = a_mn ? make_map(A.data_ptr(), M, K, A.stride(0), BK) : make_map(A.data_ptr(), K, M, A.stride(0), BM);
   const CUtensorMap tb = b_mn ? make_map(B.data_ptr(), NB, K, B.stride(0), BK) : make_map(B.data_ptr(), K, NB, B.stride(0), 128);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();

@@ -4,7 +4,41 @@
 #include <cuda_runtime.h>
 #include <torch/extension.h>
 
+#include <execinfo.h>
+#include <signal.h>
+#include <unistd.h>
+
+#include <cstdio>
+#include <cstdlib>
 #include <mutex>
+
+// Opt-in (DTB_SEGV_TRACE=1): print the native stack of a SIGSEGV to stderr,
+// then re-raise it with the default action.
+static void segv_trace(int sig) {
+  void* frames[64];
+  const int n = backtrace(frames, 64);
+  static const char msg[] = "\n[dtb] native backtrace:\n";
+  (void)!write(2, msg, sizeof(msg) - 1);
+  backtrace_symbols_fd(frames, n, 2);
+  signal(sig, SIG_DFL);
+  raise(sig);
+}
+
+static int install_segv_trace() {
+  const char* e = std::getenv("DTB_SEGV_TRACE");
+  if (e && e[0] == '1') signal(SIGSEGV, segv_trace);
+  return 0;
+}
+static int g_trace_installed = install_segv_trace();
+
+bool dtb_debug_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = std::getenv("DTB_DEBUG");
+    on = (e && e[0] == '1') ? 1 : 0;
+  }
+  return on == 1;
+}
 
 static int* g_err_words[64] = {nullptr};
 static std::mutex g_err_mu;

@@ -242,7 +242,9 @@ class FullyShardedModel(nn.Module):
         if block_units and not persistent:
             self._slots = [torch.empty(block_units[0].numel, dtype=pdt, device=dev) for _ in range(n_slots)]
         for u in self.units:
-            if u is self.units[-1] or persistent or not self._slots:
+            if self.shard_world == 1:
+                u.gathered = u.param_shard  # the shard is the whole unit: gathering is a no-op
+            elif u is self.units[-1] or persistent or not self._slots:
                 u.gathered = torch.empty(u.numel, dtype=pdt, device=dev)
             else:
                 if u.numel != block_units[0].numel:  # heterogeneous blocks: own buffer
@@ -305,6 +307,8 @@ class FullyShardedModel(nn.Module):
     # ------------------------------------------------------------ gathering
     def _gather_into(self, u: FlatUnit) -> None:
         assert u.gathered is not None and u.param_shard is not None
+        if u.gathered is u.param_shard:
+            return
         self.comm.all_gather(u.gathered, u.param_shard)
 
     def _prefetch(self, bi: int) -> None:
@@ -524,6 +528,8 @@ def count_unsharded_parameters(model: nn.Module, ctx: Any) -> int:
             for e in u.entries:
                 a, b = max(lo, e.offset), min(hi, e.offset + e.numel)
                 local += max(0, b - a)
+        if model.dp_rank >= model.shard_world:
+            local = 0  # NO_SHARD / HYBRID_SHARD replicas: count the first replica group only
         if model.tp_size > 1:
             # replicated entries exist on every TP rank: count them on tp_rank 0 only
             rep = 0
@@ -533,7 +539,7 @@ def count_unsharded_parameters(model: nn.Module, ctx: Any) -> int:
                     if e.tp_kind == "rep":
                         a, b = max(lo, e.offset), min(hi, e.offset + e.numel)
                         rep += max(0, b - a)
-            if ctx.dims.tp_rank != 0:
+            if ctx.dims.tp_rank != 0 and model.dp_rank < model.shard_world:
                 local -= rep
         t = torch.tensor([local], dtype=torch.long, device=ctx.device if ctx else "cpu")
     else:

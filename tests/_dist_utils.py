@@ -30,6 +30,7 @@ def _entry(rank: int, world: int, port: int, fn: Callable[..., None], args: tupl
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
     try:
         fn(rank, world, *args)
+        dist.barrier()
     finally:
         if dist.is_initialized():
             dist.destroy_process_group()
