@@ -60,11 +60,18 @@ class VocabParallelEmbedding(nn.Module):
         self.weight = nn.Parameter(torch.empty(self.vocab_per_partition, d_model))
         nn.init.normal_(self.weight, mean=0.0, std=0.02)
 
-    def forward(self, tokens: torch.Tensor, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    def forward(self, tokens: torch.Tensor, out_dtype: torch.dtype | None = None,
+                reduce: str = "all") -> torch.Tensor:
+        """``reduce="all"``: all-reduce the partial lookups (every rank gets every
+        token); ``"scatter"``: reduce-scatter them over the flattened tokens
+        (sequence parallelism: each rank keeps its ``tokens/tp`` rows)."""
         outside = (tokens < self.vocab_start) | (tokens >= self.vocab_end)
         local = (tokens - self.vocab_start).masked_fill(outside, 0)
         out = embedding(local, self.weight, main_grad=main_grad_of(self.weight), out_dtype=out_dtype)
         out = out.masked_fill(outside.unsqueeze(-1), 0.0)
         if self.tp_size > 1:
+            if reduce == "scatter":
+                from ..parallel.tensor_parallel import reduce_scatter_rows_autograd
+                return reduce_scatter_rows_autograd(out.reshape(-1, out.shape[-1]), self.tp_group)
             out = _SumOverTP.apply(out, self.tp_group)
         return out

@@ -84,8 +84,14 @@ class Transformer(nn.Module):
             nn.init.normal_(blk.mlp.down_proj.weight, mean=0.0, std=std)
 
     def embed(self, tokens: torch.Tensor) -> torch.Tensor:
-        h = self.tok_embeddings(tokens)
-        return tpar.sequence_scatter(h.reshape(-1, h.shape[-1]), self.tp) if tpar.sp_on(self.tp) else h
+        if not tpar.sp_on(self.tp):
+            return self.tok_embeddings(tokens)
+        if isinstance(self.tok_embeddings, VocabParallelEmbedding):
+            # partial lookups of every token, summed and split by tokens in one reduce-scatter
+            return self.tok_embeddings(tokens.reshape(-1), reduce="scatter")
+        # replicated table: look up only this rank's tokens; its gradient is partial
+        # and the sharding engine sums replicated gradients over the TP group
+        return self.tok_embeddings(tpar.sequence_slice(tokens.reshape(-1), self.tp))
 
     def head(self, h: torch.Tensor, labels: torch.Tensor | None
              ) -> tuple[torch.Tensor | None, torch.Tensor | None]:

@@ -247,6 +247,12 @@ class _AllReduceFwd(torch.autograd.Function):
         return g, None
 
 
+def reduce_scatter_rows_autograd(x2: torch.Tensor, group: dist.ProcessGroup | None) -> torch.Tensor:
+    """Sum over the group and keep this rank's rows (backward: all-gather rows)."""
+    tp = TPInfo(group, _size(group), _rank(group), sequence_parallel=True)
+    return _SeqReduceScatter.apply(x2, tp)
+
+
 def sequence_scatter(x2: torch.Tensor, tp: TPInfo | None) -> torch.Tensor:
     assert tp is not None
     return _SeqScatter.apply(x2, tp)
@@ -355,12 +361,9 @@ def vocab_parallel_head_ce(h2: torch.Tensor, weight: torch.Tensor, labels: torch
     logits = linear(x, weight, main_grad=main_grad)
     if labels is None:
         return logits, None
+    # every TP rank holds the full batch's labels; under SP the column input
+    # all-gathered the token rows, so logits cover all tokens as well
     lab = labels.reshape(-1)
-    if tp.sequence_parallel:
-        full = torch.empty(lab.shape[0] * tp.size, dtype=lab.dtype, device=lab.device)
-        parts = list(full.chunk(tp.size))
-        dist.all_gather(parts, lab.contiguous(), group=tp.group)
-        lab = torch.cat(parts)
     return None, _VocabParallelCE.apply(logits, lab, vocab_start, tp.group)
 
 

@@ -27,6 +27,8 @@ def _entry(rank: int, world: int, port: int, fn: Callable[..., None], args: tupl
     os.environ.update({"RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank),
                        "LOCAL_WORLD_SIZE": str(world), "MASTER_ADDR": "127.0.0.1",
                        "MASTER_PORT": str(port), "CUDA_VISIBLE_DEVICES": ""})
+    import torch
+    torch.set_num_threads(1)  # N ranks share the CPU cores; avoid oversubscription
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
     try:
         fn(rank, world, *args)
