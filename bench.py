@@ -263,23 +263,41 @@ def run_reference(args, n: int, rank: int, world: int) -> dict:
         "save_interval": 0, "profile_steps": 0, "backend": "nccl", "run_id": "bench_ref",
         "checkpoint_dir": tempfile.gettempdir(),
     }
-    cfg = RefConfig.from_dict(raw)
-    with contextlib.redirect_stdout(sys.stderr):
-        trainer = RefTrainer(cfg, gpu_type="h100")
-    ctx = trainer.ctx
+    note = "adamw fused=True (the reference default)"
+    for fused in (True, False):
+        raw["optimizer"]["fused"] = fused
+        cfg = RefConfig.from_dict(raw)
+        with contextlib.redirect_stdout(sys.stderr):
+            trainer = RefTrainer(cfg, gpu_type="h100")
+        ctx = trainer.ctx
 
-    def step():
-        window, wait = trainer._next_window()
-        return ref_train_step(trainer.model, window, trainer.optimizer, trainer.scheduler, ctx, cfg,
-                              gpu_type="h100", data_wait_s=wait)
+        def step():
+            window, wait = trainer._next_window()
+            return ref_train_step(trainer.model, window, trainer.optimizer, trainer.scheduler, ctx, cfg,
+                                  gpu_type="h100", data_wait_s=wait)
 
+        try:
+            with contextlib.redirect_stdout(sys.stderr):
+                step()
+            break
+        except RuntimeError as exc:
+            # torch's fused AdamW rejects the mix of DTensor (TP-sharded) and plain
+            # (replicated) parameters the reference's TP plan produces; its own
+            # config offers fused=False, which runs the same code path otherwise
+            if not fused or "mixed torch.Tensor and DTensor" not in str(exc):
+                raise
+            note = "adamw fused=False (fused AdamW raises on the reference's mixed DTensor/Tensor params)"
+            del trainer, step
+            import gc
+            gc.collect()
+            torch.cuda.empty_cache()
     with contextlib.redirect_stdout(sys.stderr):
-        for _ in range(args.warmup):
+        for _ in range(args.warmup - 1):
             step()
         with ClockSampler(rank == 0) as clk:
             dev_s, host_s = timed_loop(step, args.steps, world)
     return dict(tp=tp, dp=dp, mb=mb, dev_s=dev_s, host_s=host_s, clocks=clk.summary(n),
-                launches_per_step=0, h2d=2 * mb * SEQ * 8, d2h=8,
+                launches_per_step=0, h2d=2 * mb * SEQ * 8, d2h=8, ref_optimizer=note,
                 peak_mem=torch.cuda.max_memory_allocated())
 
 
@@ -333,6 +351,7 @@ def main() -> None:
     }
     if args.impl == "reference":
         out["impl"] = "reference"
+        out["config"]["optimizer"] = res["ref_optimizer"]
     if rank == 0:
         print(json.dumps(out), flush=True)
     _teardown()

@@ -521,11 +521,15 @@ void fwd_launch(const __nv_bfloat16* qkv, __nv_bfloat16* o, float* lse, int B, i
 }
 
 template <int HD>
-void bwd_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* o, const __nv_bfloat16* dO, const float* lse, float* Dv,
-                __nv_bfloat16* dqkv, int B, int S, int nq, int nkv, float scale, cudaStream_t st) {
+void bwd_pre_launch(const __nv_bfloat16* o, const __nv_bfloat16* dO, float* Dv, int B, int S, int nq, cudaStream_t st) {
   const long rows = (long)B * S;
   const long warps = rows * nq;
   attn_bwd_pre_kernel<HD><<<(int)((warps * 32 + 255) / 256), 256, 0, st>>>(o, dO, Dv, S, nq, rows);
+}
+
+template <int HD>
+void bwd_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* o, const __nv_bfloat16* dO, const float* lse, float* Dv,
+                __nv_bfloat16* dqkv, int B, int S, int nq, int nkv, float scale, cudaStream_t st) {
   const int smem_kv = (2 * 64 + 4 * 32) * HD * 2 + 4 * 32 * 4;
   const int smem_q = (2 * 64 + 4 * 32) * HD * 2;
   static bool cfg = false;
@@ -553,12 +557,17 @@ static void attn_check(const torch::Tensor& qkv, int64_t B, int64_t S, int64_t n
   TORCH_CHECK(qkv.size(0) == B * S && qkv.size(1) == (nq + 2 * nkv) * hd, "attention: qkv shape");
 }
 
+bool attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse, int64_t B, int64_t S, int64_t nq,
+                 int64_t nkv, int64_t hd, double scale);
+
 std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t B, int64_t S, int64_t nq, int64_t nkv, int64_t hd,
-                                    double scale) {
+                                    double scale, bool legacy) {
   attn_check(qkv, B, S, nq, nkv, hd);
   const c10::cuda::CUDAGuard g(qkv.device());
   auto o = torch::empty({B * S, nq * hd}, qkv.options());
   auto lse = torch::empty({B, nq, S}, qkv.options().dtype(at::kFloat));
+  // tcgen05/TMEM kernel (attention_tc.cu) unless the sequence is not a multiple of 128
+  if (!legacy && attn_fwd_tc(qkv, o, lse, B, S, nq, nkv, hd, scale)) return {o, lse};
   auto st = at::cuda::getCurrentCUDAStream();
   auto q = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
   auto op = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
@@ -568,8 +577,11 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t B, int64_t S, int
   return {o, lse};
 }
 
+bool attn_bwd_tc(const torch::Tensor& dO, const torch::Tensor& qkv, const float* lse, const float* Dv,
+                 torch::Tensor& dqkv, int64_t B, int64_t S, int64_t nq, int64_t nkv, int64_t hd, double scale);
+
 torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, int64_t B, int64_t S,
-                       int64_t nq, int64_t nkv, int64_t hd, double scale) {
+                       int64_t nq, int64_t nkv, int64_t hd, double scale, bool legacy) {
   attn_check(qkv, B, S, nq, nkv, hd);
   TORCH_CHECK(dO.is_contiguous() && dO.sizes() == o.sizes(), "attention bwd: dO shape");
   const c10::cuda::CUDAGuard g(qkv.device());
@@ -578,6 +590,12 @@ torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qkv, torch::Tensor o, tor
   auto st = at::cuda::getCurrentCUDAStream();
   auto cast = [](const torch::Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr()); };
   auto dq = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
+  if (hd == 128) attn::bwd_pre_launch<128>(cast(o), cast(dO), Dv.data_ptr<float>(), B, S, nq, st);
+  else attn::bwd_pre_launch<64>(cast(o), cast(dO), Dv.data_ptr<float>(), B, S, nq, st);
+  DTB_LAUNCH_CHECK();
+  // tcgen05/TMEM kernels (attention_bwd_tc.cu) unless the sequence is not a multiple of 128
+  if (!legacy && attn_bwd_tc(dO, qkv, lse.data_ptr<float>(), Dv.data_ptr<float>(), dqkv, B, S, nq, nkv, hd, scale))
+    return dqkv;
   if (hd == 128)
     attn::bwd_launch<128>(cast(qkv), cast(o), cast(dO), lse.data_ptr<float>(), Dv.data_ptr<float>(), dq, B, S, nq, nkv,
                           (float)scale, st);

@@ -1,0 +1,606 @@
+// Causal GQA flash-attention backward on tcgen05/TMEM (sm_100a), deterministic.
+//
+// Two kernels, no atomics (every output element is written by one CTA, and
+// every sum runs in a fixed order), so the backward is bit-reproducible:
+//
+// attn_bwd_dkdv_tc: CTA per (128-key tile, kv head, batch).  For every query
+//   head of the kv head's group and every 64-query tile at or after the
+//   diagonal:
+//     S^T  = K Q^T      [128 keys x 64 queries]   (TMEM, double buffered)
+//     dP^T = V dO^T     [128 x 64]                (TMEM, double buffered)
+//     P^T  = exp2(S^T * scale*log2e - lse*log2e), dS^T = P^T (dP^T - D)
+//            (4 warps, thread = key row; both written to shared memory in bf16)
+//     dV  += P^T dO     [128 x hd]                (TMEM accumulator)
+//     dK  += dS^T Q     [128 x hd]                (TMEM accumulator, * scale at the end)
+// attn_bwd_dq_tc: CTA per (128-query tile, head, batch), over 64-key tiles:
+//     S = Q K^T, dP = dO V^T, dS = P (dP - D), dQ += dS K.
+//
+// The Q / dO / K tiles are loaded once by TMA in the 128-byte-swizzled K-major
+// layout; the same bytes serve as MN-major operands (a [rows][64] swizzled
+// tile is both), so nothing is transposed.  lse and D = rowsum(dO * O) rows
+// arrive by bulk copies next to the tiles, three tiles deep; S / dP are issued
+// two tiles ahead of the products that consume P / dS.  Warp 0 loads, warp 1 owns TMEM
+// and issues MMAs, warps 2-9 (two warpgroups, each taking half of a tile's
+// columns) do the elementwise part.  Bounded waits only.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cudaTypedefs.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace dtb {
+namespace fab {
+
+constexpr float LOG2E = 1.4426950408889634f;
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// one 64-column bf16 row segment into a [rows][64] 128B-swizzled tile
+__device__ __forceinline__ void store_row64(uint8_t* tile, int r, const uint32_t (&pk)[32]) {
+#pragma unroll
+  for (int cc = 0; cc < 8; ++cc) {
+    uint4 v;
+    v.x = pk[cc * 4 + 0];
+    v.y = pk[cc * 4 + 1];
+    v.z = pk[cc * 4 + 2];
+    v.w = pk[cc * 4 + 3];
+    *reinterpret_cast<uint4*>(tile + r * 128 + ((cc ^ (r & 7)) << 4)) = v;
+  }
+}
+
+// columns [32*half, 32*half + 32) of row r of a [rows][64] swizzled tile
+__device__ __forceinline__ void store_row32(uint8_t* tile, int r, int half, const uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int cc = half * 4 + q;
+    uint4 v;
+    v.x = pk[q * 4 + 0];
+    v.y = pk[q * 4 + 1];
+    v.z = pk[q * 4 + 2];
+    v.w = pk[q * 4 + 3];
+    *reinterpret_cast<uint4*>(tile + r * 128 + ((cc ^ (r & 7)) << 4)) = v;
+  }
+}
+
+struct BwdArgs {
+  const float* lse;   // [B, nq, S] natural log
+  const float* Dv;    // [B, nq, S]
+  __nv_bfloat16* dqkv;
+  int S, nq, nkv;
+  float scale, scale_log2;
+  int* err;
+};
+
+// ============================================================== dK / dV
+template <int HD>
+struct SmKV {
+  static constexpr int KV_TILE = 128 * HD * 2;   // K or V: [hd/64][128 rows][128 B]
+  static constexpr int QT = 64 * HD * 2;         // Q or dO tile: [hd/64][64 rows][128 B]
+  static constexpr int K_OFF = 0;
+  static constexpr int V_OFF = K_OFF + KV_TILE;
+  static constexpr int NS = 3;                   // Q / dO / lse / D load stages
+  static constexpr int Q_OFF = V_OFF + KV_TILE;
+  static constexpr int O_OFF = Q_OFF + NS * QT;  // dO
+  static constexpr int P_OFF = O_OFF + NS * QT;  // P^T [128][64] bf16
+  static constexpr int DS_OFF = P_OFF + 16384;   // dS^T
+  static constexpr int LD_OFF = DS_OFF + 16384;  // NS x (lse[64], D[64]) floats
+  static constexpr int BAR_OFF = LD_OFF + NS * 512;
+  static constexpr int N_BARS = 14;
+  static constexpr int TOTAL = BAR_OFF + N_BARS * 8 + 16 + 1024;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(320, 1)
+    attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_q,
+                            const __grid_constant__ CUtensorMap tm_do, const BwdArgs a) {
+  using L = SmKV<HD>;
+  constexpr int BKV = 128, BQ = 64;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR_OFF);
+  constexpr int NS = L::NS;
+  uint64_t* kv_full = bars + 0;
+  uint64_t* q_full = bars + 1;   // [NS]
+  uint64_t* q_empty = bars + 4;  // [NS]
+  uint64_t* s_full = bars + 7;   // [2]  S^T and dP^T ready
+  uint64_t* s_empty = bars + 9;  // [2]
+  uint64_t* p_full = bars + 11;  // P^T / dS^T written
+  uint64_t* p_done = bars + 12;  // dV / dK MMAs of that tile finished
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + L::N_BARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkb = a.S / BKV;
+  const int kb = nkb - 1 - blockIdx.x;  // tiles near the end have the least work: start the others first
+  const int hk = blockIdx.y, b = blockIdx.z;
+  const int grp = a.nq / a.nkv;
+  const int kv0 = kb * BKV;
+  const int q_first = kv0 / BQ;
+  const int nqt = a.S / BQ - q_first;
+  const int total = nqt * grp;
+  const int row0 = b * a.S;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 256);
+    }
+    mbar_init(p_full, 256);
+    mbar_init(p_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  // TMEM: S^T[2] at 0/64, dP^T[2] at 128/192, dV at 256, dK at 256+HD
+  const uint32_t t_s[2] = {tmem, tmem + 64}, t_dp[2] = {tmem + 128, tmem + 192};
+  const uint32_t t_dv = tmem + 256, t_dk = tmem + 256 + HD;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * L::KV_TILE);
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c) {
+        tma_load_2d(sm + L::K_OFF + c * 16384, &tm_kv, kv_full, (a.nq + hk) * HD + c * 64, row0 + kv0);
+        tma_load_2d(sm + L::V_OFF + c * 16384, &tm_kv, kv_full, (a.nq + a.nkv + hk) * HD + c * 64, row0 + kv0);
+      }
+      for (int it = 0; it < total; ++it) {
+        const int st = it % NS;
+        if (*abort_flag || !mbar_wait(&q_empty[st], ((it / NS) & 1) ^ 1, a.err)) {
+          *abort_flag = 1;
+          break;
+        }
+        const int hh = hk * grp + it / nqt;
+        const int q0 = (q_first + it % nqt) * BQ;
+        mbar_arrive_expect_tx(&q_full[st], 2 * L::QT + 512);
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c) {
+          tma_load_2d(sm + L::Q_OFF + st * L::QT + c * 8192, &tm_q, &q_full[st], hh * HD + c * 64, row0 + q0);
+          tma_load_2d(sm + L::O_OFF + st * L::QT + c * 8192, &tm_do, &q_full[st], hh * HD + c * 64, row0 + q0);
+        }
+        const long li = ((long)b * a.nq + hh) * a.S + q0;
+        bulk_load(sm + L::LD_OFF + st * 512, a.lse + li, 256, &q_full[st]);
+        bulk_load(sm + L::LD_OFF + st * 512 + 256, a.Dv + li, 256, &q_full[st]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_S = idesc_bf16(128, 64, false, false);   // S^T, dP^T
+      constexpr uint32_t ID_G = idesc_bf16(128, HD, false, true);    // dV, dK (B = dO / Q as MN-major)
+      const uint32_t k0 = smem_u32(sm + L::K_OFF), v0 = smem_u32(sm + L::V_OFF);
+      const uint32_t pt = smem_u32(sm + L::P_OFF), dst = smem_u32(sm + L::DS_OFF);
+      bool ok = mbar_wait(kv_full, 0, a.err);
+      auto issue_s = [&](int it) -> bool {
+        const int st = it % NS, tb = it & 1;
+        if (!mbar_wait(&q_full[st], (it / NS) & 1, a.err)) return false;
+        if (!mbar_wait(&s_empty[tb], ((it >> 1) & 1) ^ 1, a.err)) return false;
+        tc_fence_after();
+        const uint32_t q0 = smem_u32(sm + L::Q_OFF + st * L::QT), o0 = smem_u32(sm + L::O_OFF + st * L::QT);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t oa = (kk >> 2) * 16384 + (kk & 3) * 32;  // K / V atoms: 128 rows
+          const uint32_t ob = (kk >> 2) * 8192 + (kk & 3) * 32;   // Q / dO atoms: 64 rows
+          umma_bf16(t_s[tb], sdesc_sw128(k0 + oa, 16, 1024), sdesc_sw128(q0 + ob, 16, 1024), ID_S, kk != 0);
+          umma_bf16(t_dp[tb], sdesc_sw128(v0 + oa, 16, 1024), sdesc_sw128(o0 + ob, 16, 1024), ID_S, kk != 0);
+        }
+        umma_commit(&s_full[tb]);
+        return true;
+      };
+      // S^T / dP^T run two tiles ahead of the dV / dK products
+      if (ok && total > 0) ok = issue_s(0);
+      if (ok && total > 1) ok = issue_s(1);
+      for (int it = 0; it < total && ok && !*abort_flag; ++it) {
+        if (!mbar_wait(p_full, it & 1, a.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int st = it % NS;
+        const uint32_t q0 = smem_u32(sm + L::Q_OFF + st * L::QT), o0 = smem_u32(sm + L::O_OFF + st * L::QT);
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk) {
+          const uint32_t pa = kk * 32;        // [128][64] K-major A tile
+          const uint32_t gb = kk * 2048;      // 16 query rows of the MN-major B tile
+          umma_bf16(t_dv, sdesc_sw128(pt + pa, 16, 1024), sdesc_sw128(o0 + gb, 8192, 1024), ID_G, (it | kk) != 0);
+          umma_bf16(t_dk, sdesc_sw128(dst + pa, 16, 1024), sdesc_sw128(q0 + gb, 8192, 1024), ID_G, (it | kk) != 0);
+        }
+        umma_commit(&q_empty[st]);
+        umma_commit(p_done);
+        if (it + 2 < total && !issue_s(it + 2)) {
+          ok = false;
+          break;
+        }
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    // warps 2-9: two warpgroups; group g handles columns [32g, 32g+32) of every row
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int c0 = half * 32;
+    const int r = quad * 32 + lane;  // key row within the tile
+    const int kr = kv0 + r;
+    const uint32_t lo = (uint32_t)(quad * 32) << 16;
+    bool ok = true;
+    for (int it = 0; it < total; ++it) {
+      const int tb = it & 1, st = it % NS;
+      if (*abort_flag || !mbar_wait(&s_full[tb], (it >> 1) & 1, a.err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[32], dp[32];
+      tmem_ld32(t_s[tb] + lo + c0, s);
+      tmem_ld32(t_dp[tb] + lo + c0, dp);
+      tc_fence_before();
+      mbar_arrive(&s_empty[tb]);
+      // lse / D rows of this tile arrived with the tile's bulk copies (already
+      // complete: the MMA warp waited for them); waiting here makes the async
+      // writes visible to these threads
+      if (!mbar_wait(&q_full[st], (it / NS) & 1, a.err)) {
+        ok = false;
+        break;
+      }
+      const float* Ls = reinterpret_cast<const float*>(sm + L::LD_OFF + st * 512);
+      const float* Ds = Ls + 64;
+      const int q0 = (q_first + it % nqt) * BQ;
+      uint32_t pp[16], pd[16];
+#pragma unroll
+      for (int c = 0; c < 32; c += 2) {
+        float p[2], d[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int qc = c0 + c + e;
+          float v = exp2f(s[c + e] * a.scale_log2 - Ls[qc] * LOG2E);
+          if (q0 + qc < kr) v = 0.f;
+          p[e] = v;
+          d[e] = v * (dp[c + e] - Ds[qc]);
+        }
+        pp[c / 2] = pack_bf16x2(p[0], p[1]);
+        pd[c / 2] = pack_bf16x2(d[0], d[1]);
+      }
+      if (it > 0) {  // the previous tile's dV/dK MMAs read the P^T / dS^T buffers
+        if (!mbar_wait(p_done, (it - 1) & 1, a.err)) {
+          ok = false;
+          break;
+        }
+      }
+      store_row32(sm + L::P_OFF, r, half, pp);
+      store_row32(sm + L::DS_OFF, r, half, pd);
+      fence_proxy_async_smem();
+      mbar_arrive(p_full);
+    }
+    if (ok && total > 0 && mbar_wait(p_done, (total - 1) & 1, a.err)) {
+      tc_fence_after();
+      const long ld = (long)(a.nq + 2 * a.nkv) * HD;
+      __nv_bfloat16* gk = a.dqkv + ((long)row0 + kr) * ld + (a.nq + hk) * HD;
+      __nv_bfloat16* gv = a.dqkv + ((long)row0 + kr) * ld + (a.nq + a.nkv + hk) * HD;
+#pragma unroll 1
+      for (int c = half * (HD / 2); c < (half + 1) * (HD / 2); c += 32) {
+        float dk[32], dv[32];
+        tmem_ld32(t_dk + lo + c, dk);
+        tmem_ld32(t_dv + lo + c, dv);
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 wk, wv;
+          wk.x = pack_bf16x2(dk[i] * a.scale, dk[i + 1] * a.scale);
+          wk.y = pack_bf16x2(dk[i + 2] * a.scale, dk[i + 3] * a.scale);
+          wk.z = pack_bf16x2(dk[i + 4] * a.scale, dk[i + 5] * a.scale);
+          wk.w = pack_bf16x2(dk[i + 6] * a.scale, dk[i + 7] * a.scale);
+          wv.x = pack_bf16x2(dv[i], dv[i + 1]);
+          wv.y = pack_bf16x2(dv[i + 2], dv[i + 3]);
+          wv.z = pack_bf16x2(dv[i + 4], dv[i + 5]);
+          wv.w = pack_bf16x2(dv[i + 6], dv[i + 7]);
+          *reinterpret_cast<uint4*>(gk + c + i) = wk;
+          *reinterpret_cast<uint4*>(gv + c + i) = wv;
+        }
+      }
+    } else {
+      *abort_flag = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// ============================================================== dQ
+template <int HD>
+struct SmQ {
+  static constexpr int QT = 128 * HD * 2;        // Q or dO: [hd/64][128][128 B]
+  static constexpr int KT = 64 * HD * 2;         // K or V tile: [hd/64][64][128 B]
+  static constexpr int Q_OFF = 0;
+  static constexpr int O_OFF = Q_OFF + QT;
+  static constexpr int NS = 3;                   // K / V load stages
+  static constexpr int K_OFF = O_OFF + QT;
+  static constexpr int V_OFF = K_OFF + NS * KT;
+  static constexpr int DS_OFF = V_OFF + NS * KT;  // dS [128][64]
+  static constexpr int BAR_OFF = DS_OFF + 16384;
+  static constexpr int N_BARS = 14;
+  static constexpr int TOTAL = BAR_OFF + N_BARS * 8 + 16 + 1024;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(320, 1)
+    attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_q128, const __grid_constant__ CUtensorMap tm_do128,
+                          const __grid_constant__ CUtensorMap tm_kv64, const BwdArgs a) {
+  using L = SmQ<HD>;
+  constexpr int BQ = 128, BKV = 64;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR_OFF);
+  constexpr int NS = L::NS;
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [NS]
+  uint64_t* kv_empty = bars + 4;  // [NS]
+  uint64_t* s_full = bars + 7;    // [2]
+  uint64_t* s_empty = bars + 9;   // [2]
+  uint64_t* p_full = bars + 11;
+  uint64_t* p_done = bars + 12;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + L::N_BARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqb = a.S / BQ;
+  const int qb = nqb - 1 - blockIdx.x;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (a.nq / a.nkv);
+  const int q0 = qb * BQ;
+  const int nkt = (q0 + BQ) / BKV;
+  const int row0 = b * a.S;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 256);
+    }
+    mbar_init(p_full, 256);
+    mbar_init(p_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const uint32_t t_s[2] = {tmem, tmem + 64}, t_dp[2] = {tmem + 128, tmem + 192};
+  const uint32_t t_dq = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, 2 * L::QT);
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c) {
+        tma_load_2d(sm + L::Q_OFF + c * 16384, &tm_q128, q_full, h * HD + c * 64, row0 + q0);
+        tma_load_2d(sm + L::O_OFF + c * 16384, &tm_do128, q_full, h * HD + c * 64, row0 + q0);
+      }
+      for (int j = 0; j < nkt; ++j) {
+        const int st = j % NS;
+        if (*abort_flag || !mbar_wait(&kv_empty[st], ((j / NS) & 1) ^ 1, a.err)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&kv_full[st], 2 * L::KT);
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c) {
+          tma_load_2d(sm + L::K_OFF + st * L::KT + c * 8192, &tm_kv64, &kv_full[st], (a.nq + hk) * HD + c * 64,
+                      row0 + j * BKV);
+          tma_load_2d(sm + L::V_OFF + st * L::KT + c * 8192, &tm_kv64, &kv_full[st],
+                      (a.nq + a.nkv + hk) * HD + c * 64, row0 + j * BKV);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_S = idesc_bf16(128, 64, false, false);
+      constexpr uint32_t ID_Q = idesc_bf16(128, HD, false, true);
+      const uint32_t qa = smem_u32(sm + L::Q_OFF), oa = smem_u32(sm + L::O_OFF), dsa = smem_u32(sm + L::DS_OFF);
+      bool ok = mbar_wait(q_full, 0, a.err);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % NS, tb = j & 1;
+        if (!mbar_wait(&kv_full[st], (j / NS) & 1, a.err)) return false;
+        if (!mbar_wait(&s_empty[tb], ((j >> 1) & 1) ^ 1, a.err)) return false;
+        tc_fence_after();
+        const uint32_t k0 = smem_u32(sm + L::K_OFF + st * L::KT), v0 = smem_u32(sm + L::V_OFF + st * L::KT);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t o128 = (kk >> 2) * 16384 + (kk & 3) * 32;
+          const uint32_t o64 = (kk >> 2) * 8192 + (kk & 3) * 32;
+          umma_bf16(t_s[tb], sdesc_sw128(qa + o128, 16, 1024), sdesc_sw128(k0 + o64, 16, 1024), ID_S, kk != 0);
+          umma_bf16(t_dp[tb], sdesc_sw128(oa + o128, 16, 1024), sdesc_sw128(v0 + o64, 16, 1024), ID_S, kk != 0);
+        }
+        umma_commit(&s_full[tb]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && nkt > 1) ok = issue_s(1);
+      for (int j = 0; j < nkt && ok && !*abort_flag; ++j) {
+        if (!mbar_wait(p_full, j & 1, a.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int st = j % NS;
+        const uint32_t k0 = smem_u32(sm + L::K_OFF + st * L::KT);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk)
+          umma_bf16(t_dq, sdesc_sw128(dsa + kk * 32, 16, 1024), sdesc_sw128(k0 + kk * 2048, 8192, 1024), ID_Q,
+                    (j | kk) != 0);
+        umma_commit(&kv_empty[st]);
+        umma_commit(p_done);
+        if (j + 2 < nkt && !issue_s(j + 2)) {
+          ok = false;
+          break;
+        }
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;  // warpgroup: columns [32*half, 32*half + 32)
+    const int c0 = half * 32;
+    const int r = quad * 32 + lane;
+    const int qr = q0 + r;
+    const uint32_t lo = (uint32_t)(quad * 32) << 16;
+    const long li = ((long)b * a.nq + h) * a.S + qr;
+    const float L2 = a.lse[li] * LOG2E, Dr = a.Dv[li];
+    bool ok = true;
+    for (int j = 0; j < nkt; ++j) {
+      const int tb = j & 1;
+      if (*abort_flag || !mbar_wait(&s_full[tb], (j >> 1) & 1, a.err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[32], dp[32];
+      tmem_ld32(t_s[tb] + lo + c0, s);
+      tmem_ld32(t_dp[tb] + lo + c0, dp);
+      tc_fence_before();
+      mbar_arrive(&s_empty[tb]);
+      uint32_t pd[16];
+#pragma unroll
+      for (int c = 0; c < 32; c += 2) {
+        float d[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int kc = j * BKV + c0 + c + e;
+          float p = exp2f(s[c + e] * a.scale_log2 - L2);
+          if (kc > qr) p = 0.f;
+          d[e] = p * (dp[c + e] - Dr);
+        }
+        pd[c / 2] = pack_bf16x2(d[0], d[1]);
+      }
+      if (j > 0) {
+        if (!mbar_wait(p_done, (j - 1) & 1, a.err)) {
+          ok = false;
+          break;
+        }
+      }
+      store_row32(sm + L::DS_OFF, r, half, pd);
+      fence_proxy_async_smem();
+      mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait(p_done, (nkt - 1) & 1, a.err)) {
+      tc_fence_after();
+      const long ld = (long)(a.nq + 2 * a.nkv) * HD;
+      __nv_bfloat16* gq = a.dqkv + ((long)row0 + qr) * ld + h * HD;
+#pragma unroll 1
+      for (int c = half * (HD / 2); c < (half + 1) * (HD / 2); c += 32) {
+        float dq[32];
+        tmem_ld32(t_dq + lo + c, dq);
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 w;
+          w.x = pack_bf16x2(dq[i] * a.scale, dq[i + 1] * a.scale);
+          w.y = pack_bf16x2(dq[i + 2] * a.scale, dq[i + 3] * a.scale);
+          w.z = pack_bf16x2(dq[i + 4] * a.scale, dq[i + 5] * a.scale);
+          w.w = pack_bf16x2(dq[i + 6] * a.scale, dq[i + 7] * a.scale);
+          *reinterpret_cast<uint4*>(gq + c + i) = w;
+        }
+      }
+    } else {
+      *abort_flag = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    DTB_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    DTB_CHECK(q == cudaDriverEntryPointSuccess && p, "cuTensorMapEncodeTiled not available");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+static CUtensorMap map2d(const void* base, long rows, long cols, int box_rows) {
+  static thread_local bool bound = false;
+  if (!bound) {
+    DTB_CUDA(cudaFree(nullptr));  // bind the primary context on this (autograd) thread
+    bound = true;
+  }
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  DTB_CHECK(r == CUDA_SUCCESS, "attention backward tensor map encode failed (%d)", (int)r);
+  return m;
+}
+
+template <int HD>
+void bwd_tc_launch(const torch::Tensor& qkv, const torch::Tensor& dO, const float* lse, const float* Dv,
+                   torch::Tensor& dqkv, int B, int S, int nq, int nkv, float scale) {
+  const long rows = (long)B * S, cols = (long)(nq + 2 * nkv) * HD, ocols = (long)nq * HD;
+  const CUtensorMap kv128 = map2d(qkv.data_ptr(), rows, cols, 128);
+  const CUtensorMap q64 = map2d(qkv.data_ptr(), rows, cols, 64);
+  const CUtensorMap do64 = map2d(dO.data_ptr(), rows, ocols, 64);
+  const CUtensorMap do128 = map2d(dO.data_ptr(), rows, ocols, 128);
+  static bool cfg = false;
+  if (!cfg) {
+    DTB_CUDA(cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  SmKV<HD>::TOTAL));
+    DTB_CUDA(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  SmQ<HD>::TOTAL));
+    cfg = true;
+  }
+  BwdArgs args{lse, Dv, reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), S, nq, nkv, scale, scale * LOG2E,
+               dtb_error_word()};
+  auto st = at::cuda::getCurrentCUDAStream();
+  attn_bwd_dkdv_tc_kernel<HD><<<dim3(S / 128, nkv, B), 320, SmKV<HD>::TOTAL, st>>>(kv128, q64, do64, args);
+  DTB_LAUNCH_CHECK();
+  attn_bwd_dq_tc_kernel<HD><<<dim3(S / 128, nq, B), 320, SmQ<HD>::TOTAL, st>>>(kv128, do128, q64, args);
+  DTB_LAUNCH_CHECK();
+}
+
+}  // namespace fab
+}  // namespace dtb
+
+// dK/dV and dQ on tcgen05 (D = rowsum(dO*O) already in Dv).  Returns false
+// when the shape is not covered (then the caller uses the mma.sync kernels).
+bool attn_bwd_tc(const torch::Tensor& dO, const torch::Tensor& qkv, const float* lse, const float* Dv,
+                 torch::Tensor& dqkv, int64_t B, int64_t S, int64_t nq, int64_t nkv, int64_t hd, double scale) {
+  if (S % 128 != 0 || (hd != 64 && hd != 128)) return false;
+  if (hd == 128)
+    dtb::fab::bwd_tc_launch<128>(qkv, dO, lse, Dv, dqkv, (int)B, (int)S, (int)nq, (int)nkv, (float)scale);
+  else
+    dtb::fab::bwd_tc_launch<64>(qkv, dO, lse, Dv, dqkv, (int)B, (int)S, (int)nq, (int)nkv, (float)scale);
+  return true;
+}

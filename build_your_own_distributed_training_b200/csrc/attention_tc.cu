@@ -1,0 +1,393 @@
+// Causal GQA flash-attention forward on the 5th-generation tensor cores
+// (tcgen05 + TMEM + TMA), sm_100a.
+//
+// One CTA per (128-row query tile, head, batch); 6 warps:
+//   warp 0     TMA producer: the Q tile once, then K and V tiles (128 keys)
+//              into a 2-deep ring, straight from the packed qkv projection;
+//   warp 1     owns TMEM (512 columns: two 128-column S buffers + the O
+//              accumulator) and one thread issues the MMAs:
+//                S_j = Q K_j^T   (M=128, N=128, K=hd; both operands K-major)
+//                O  += P_j V_j   (M=128, N=hd,  K=128; V is MN-major)
+//              S_{j+1} is computed while the softmax warps work on S_j;
+//   warps 2-5  softmax: thread t owns query row t (TMEM lane t), reads its S
+//              row with tcgen05.ld, applies the causal mask and the online
+//              softmax in exp2 form, writes P_j in bf16 to shared memory in the
+//              128-byte-swizzled K-major layout the MMA reads, and finally
+//              normalises O and writes it out with the log-sum-exp.
+//
+// O is rescaled only when a row's running maximum grows by more than 8 (in
+// log2 units): until then P = exp2(s - m_stale) <= 2^8, which fp32 and bf16
+// hold exactly as well, and the final 1/l uses the same stale maximum, so
+// the result is the same softmax.
+//
+// Every mbarrier wait is bounded (common.cuh); no TMA multicast.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cudaTypedefs.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace dtb {
+namespace fa {
+
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr int BM = 128, BN = 128;
+constexpr float RESCALE_THRESHOLD = 8.f;
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+template <int HD>
+struct Smem {
+  static constexpr int Q_BYTES = BM * HD * 2;           // [hd/64 atoms][128 rows][128 B]
+  static constexpr int K_BYTES = BN * HD * 2;
+  static constexpr int V_BYTES = BN * HD * 2;           // [2 kv chunks][hd/64][64 rows][128 B]
+  static constexpr int P_BYTES = BM * BN * 2;           // [2 atoms][128 rows][128 B]
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_OFF + Q_BYTES;         // 2 stages
+  static constexpr int V_OFF = K_OFF + 2 * K_BYTES;     // 2 stages
+  static constexpr int P_OFF = V_OFF + 2 * V_BYTES;
+  static constexpr int BAR_OFF = P_OFF + P_BYTES;
+  static constexpr int N_BARS = 16;
+  static constexpr int TOTAL = BAR_OFF + N_BARS * 8 + 16 + 1024;
+};
+
+struct FwdArgs {
+  __nv_bfloat16* out;
+  float* lse;
+  int S, nq, nkv;
+  float scale_log2;
+  int* err;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qk, const __grid_constant__ CUtensorMap tm_v,
+                       const FwdArgs a) {
+  using L = Smem<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;     // [2]
+  uint64_t* k_empty = bars + 3;    // [2]
+  uint64_t* s_full = bars + 5;     // [2]
+  uint64_t* s_empty = bars + 7;    // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* o_done = bars + 10;
+  uint64_t* v_full = bars + 11;    // [2]
+  uint64_t* v_empty = bars + 13;   // [2]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + L::N_BARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqb = a.S / BM;
+  const int qb = nqb - 1 - blockIdx.x;  // longest rows first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (a.nq / a.nkv);
+  const int nkb = qb + 1;               // kv tiles 0..qb (causal, BN == BM)
+  const int row0 = b * a.S;             // first packed row of this sequence
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_qk);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const uint32_t t_s[2] = {tmem, tmem + 128};
+  const uint32_t t_o = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // Q tile: hd/64 boxes of [128 rows x 64]
+      mbar_arrive_expect_tx(q_full, L::Q_BYTES);
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c)
+        tma_load_2d(sm + L::Q_OFF + c * 16384, &tm_qk, q_full, h * HD + c * 64, row0 + qb * BM);
+      // K and V rings are separate: K_{j} only waits for S_{j-2} to finish,
+      // not for the PV product that still reads V_{j-2}
+      for (int j = 0; j < nkb; ++j) {
+        const int st = j & 1;
+        const uint32_t par = ((j >> 1) & 1) ^ 1;
+        if (*abort_flag || !mbar_wait(&k_empty[st], par, a.err)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&k_full[st], L::K_BYTES);
+        uint8_t* sk = sm + L::K_OFF + st * L::K_BYTES;
+        uint8_t* sv = sm + L::V_OFF + st * L::V_BYTES;
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c)
+          tma_load_2d(sk + c * 16384, &tm_qk, &k_full[st], (a.nq + hk) * HD + c * 64, row0 + j * BN);
+        if (*abort_flag || !mbar_wait(&v_empty[st], par, a.err)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[st], L::V_BYTES);
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+          for (int c = 0; c < HD / 64; ++c)
+            tma_load_2d(sv + i * (HD / 64) * 8192 + c * 8192, &tm_v, &v_full[st], (a.nq + a.nkv + hk) * HD + c * 64,
+                        row0 + j * BN + i * 64);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_S = idesc_bf16(BM, BN, false, false);
+      constexpr uint32_t ID_O = idesc_bf16(BM, HD, false, true);
+      const uint32_t q0 = smem_u32(sm + L::Q_OFF);
+      const uint32_t p0 = smem_u32(sm + L::P_OFF);
+      bool ok = mbar_wait(q_full, 0, a.err);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!mbar_wait(&k_full[st], (j >> 1) & 1, a.err)) return false;
+        if (!mbar_wait(&s_empty[st], ((j >> 1) & 1) ^ 1, a.err)) return false;
+        tc_fence_after();
+        const uint32_t k0 = smem_u32(sm + L::K_OFF + st * L::K_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_bf16(t_s[st], sdesc_sw128(q0 + off, 16, 1024), sdesc_sw128(k0 + off, 16, 1024), ID_S, kk != 0);
+        }
+        umma_commit(&s_full[st]);
+        umma_commit(&k_empty[st]);
+        return true;
+      };
+      // S runs two tiles ahead of PV
+      if (ok) ok = issue_s(0);
+      if (ok && nkb > 1) ok = issue_s(1);
+      for (int j = 0; j < nkb && ok && !*abort_flag; ++j) {
+        // P_j written (and O rescaled) by the softmax warps
+        if (!mbar_wait(p_full, j & 1, a.err)) {
+          ok = false;
+          break;
+        }
+        const int st = j & 1;
+        if (!mbar_wait(&v_full[st], (j >> 1) & 1, a.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t v0 = smem_u32(sm + L::V_OFF + st * L::V_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint32_t pa = p0 + (kk >> 2) * 16384 + (kk & 3) * 32;
+          const uint32_t vb = v0 + (kk >> 2) * (HD / 64) * 8192 + (kk & 3) * 2048;
+          umma_bf16(t_o, sdesc_sw128(pa, 16, 1024), sdesc_sw128(vb, 8192, 1024), ID_O, (j | kk) != 0);
+        }
+        umma_commit(&v_empty[st]);
+        umma_commit(o_done);
+        if (j + 2 < nkb && !issue_s(j + 2)) {
+          ok = false;
+          break;
+        }
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warps
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;          // row within the tile == TMEM lane
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    uint8_t* P = sm + L::P_OFF;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkb; ++j) {
+      const int st = j & 1;
+      if (*abort_flag || !mbar_wait(&s_full[st], (j >> 1) & 1, a.err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[BN];
+#pragma unroll
+      for (int c = 0; c < BN; c += 32) tmem_ld32(t_s[st] + lane_off + c, *reinterpret_cast<float(*)[32]>(&s[c]));
+      tc_fence_before();
+      mbar_arrive(&s_empty[st]);  // S buffer free for S_{j+2}
+      const bool diag = (j == qb);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        float v = s[c] * a.scale_log2;
+        if (diag && c > r) v = -INFINITY;
+        s[c] = v;
+        mx = fmaxf(mx, v);
+      }
+      float alpha = 1.f;
+      bool rescale = false;
+      if (mx > m_used + RESCALE_THRESHOLD) {
+        alpha = (m_used == -INFINITY) ? 0.f : exp2f(m_used - mx);
+        rescale = (m_used != -INFINITY);
+        m_used = mx;
+      }
+      float rs = 0.f;
+      uint32_t pk[BN / 2];
+#pragma unroll
+      for (int c = 0; c < BN; c += 2) {
+        const float p0 = exp2f(s[c] - m_used), p1 = exp2f(s[c + 1] - m_used);
+        rs += p0 + p1;
+        pk[c / 2] = pack_bf16x2(p0, p1);
+      }
+      l = l * alpha + rs;
+      // PV_{j-1} must be finished: it reads the P buffer and accumulates O
+      if (j > 0) {
+        if (!mbar_wait(o_done, (j - 1) & 1, a.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      if (__any_sync(0xffffffffu, rescale)) {
+        const float f = rescale ? alpha : 1.f;
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+          float o[32];
+          tmem_ld32(t_o + lane_off + c, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= f;
+          tmem_st32(t_o + lane_off + c, o);
+        }
+        tmem_st_wait();
+      }
+      // P row r -> two 64-column atoms, 16-byte chunks XOR-swizzled by (r % 8)
+#pragma unroll
+      for (int ch = 0; ch < BN / 8; ++ch) {
+        const int atom = ch >> 3, cc = ch & 7;
+        uint4 v;
+        v.x = pk[ch * 4 + 0];
+        v.y = pk[ch * 4 + 1];
+        v.z = pk[ch * 4 + 2];
+        v.w = pk[ch * 4 + 3];
+        *reinterpret_cast<uint4*>(P + atom * 16384 + r * 128 + ((cc ^ (r & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait(o_done, (nkb - 1) & 1, a.err)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      const long orow = (long)row0 + qb * BM + r;
+      __nv_bfloat16* op = a.out + orow * (long)a.nq * HD + h * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        float o[32];
+        tmem_ld32(t_o + lane_off + c, o);
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 w;
+          w.x = pack_bf16x2(o[i] * inv, o[i + 1] * inv);
+          w.y = pack_bf16x2(o[i + 2] * inv, o[i + 3] * inv);
+          w.z = pack_bf16x2(o[i + 4] * inv, o[i + 5] * inv);
+          w.w = pack_bf16x2(o[i + 6] * inv, o[i + 7] * inv);
+          *reinterpret_cast<uint4*>(op + c + i) = w;
+        }
+      }
+      a.lse[((long)b * a.nq + h) * a.S + qb * BM + r] = (m_used + log2f(l)) / LOG2E;
+    } else {
+      *abort_flag = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    DTB_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    DTB_CHECK(q == cudaDriverEntryPointSuccess && p, "cuTensorMapEncodeTiled not available");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+static CUtensorMap qkv_map(const void* base, long rows, long cols, int box_rows) {
+  static thread_local bool bound = false;
+  if (!bound) {
+    DTB_CUDA(cudaFree(nullptr));  // the encode is a driver call: bind the primary context on this thread
+    bound = true;
+  }
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  DTB_CHECK(r == CUDA_SUCCESS, "attention tensor map encode failed (%d)", (int)r);
+  return m;
+}
+
+template <int HD>
+void fwd_tc_launch(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse, int B, int S, int nq, int nkv,
+                   float scale) {
+  using L = Smem<HD>;
+  const long rows = (long)B * S, cols = (long)(nq + 2 * nkv) * HD;
+  const CUtensorMap tqk = qkv_map(qkv.data_ptr(), rows, cols, 128);
+  const CUtensorMap tv = qkv_map(qkv.data_ptr(), rows, cols, 64);
+  static bool cfg = false;
+  if (!cfg) {
+    DTB_CUDA(cudaFuncSetAttribute(attn_fwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    cfg = true;
+  }
+  FwdArgs args{reinterpret_cast<__nv_bfloat16*>(o.data_ptr()), lse.data_ptr<float>(), S, nq, nkv, scale * LOG2E,
+               dtb_error_word()};
+  attn_fwd_tc_kernel<HD><<<dim3(S / BM, nq, B), 192, L::TOTAL, at::cuda::getCurrentCUDAStream()>>>(tqk, tv, args);
+  DTB_LAUNCH_CHECK();
+}
+
+}  // namespace fa
+}  // namespace dtb
+
+// Used by attn_fwd when head_dim is 64/128 and seq_len % 128 == 0.
+bool attn_fwd_tc(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse, int64_t B, int64_t S, int64_t nq,
+                 int64_t nkv, int64_t hd, double scale) {
+  if (S % 128 != 0 || (hd != 64 && hd != 128)) return false;
+  const c10::cuda::CUDAGuard g(qkv.device());
+  if (hd == 128) dtb::fa::fwd_tc_launch<128>(qkv, o, lse, (int)B, (int)S, (int)nq, (int)nkv, (float)scale);
+  else dtb::fa::fwd_tc_launch<64>(qkv, o, lse, (int)B, (int)S, (int)nq, (int)nkv, (float)scale);
+  return true;
+}

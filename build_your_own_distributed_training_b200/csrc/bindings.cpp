@@ -17,9 +17,9 @@ void adamw(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, t
            c10::optional<torch::Tensor> clip, double lr, double b1, double b2, double eps, double wd, int64_t step);
 torch::Tensor sumsq(torch::Tensor x);
 std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t B, int64_t S, int64_t nq, int64_t nkv, int64_t hd,
-                                    double scale);
+                                    double scale, bool legacy);
 torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, int64_t B, int64_t S,
-                       int64_t nq, int64_t nkv, int64_t hd, double scale);
+                       int64_t nq, int64_t nkv, int64_t hd, double scale, bool legacy);
 int64_t device_error();
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -35,7 +35,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cross_entropy_fwd", &cross_entropy_fwd);
   m.def("adamw", &adamw);
   m.def("sumsq", &sumsq);
-  m.def("attn_fwd", &attn_fwd);
-  m.def("attn_bwd", &attn_bwd);
+  m.def("attn_fwd", &attn_fwd, py::arg("qkv"), py::arg("B"), py::arg("S"), py::arg("nq"), py::arg("nkv"),
+        py::arg("hd"), py::arg("scale"), py::arg("legacy") = false);
+  m.def("attn_bwd", &attn_bwd, py::arg("dO"), py::arg("qkv"), py::arg("o"), py::arg("lse"), py::arg("B"),
+        py::arg("S"), py::arg("nq"), py::arg("nkv"), py::arg("hd"), py::arg("scale"), py::arg("legacy") = false);
   m.def("device_error", &device_error, "read and clear the device error word");
 }

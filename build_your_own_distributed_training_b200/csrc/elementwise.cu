@@ -295,12 +295,39 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
   }
   const float step = lr / bc1;
   const float decay = 1.f - lr * wd;
-  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    const float gi = g[i] * coef;
-    float pi = p[i] * decay;
-    const float mi = b1 * m[i] + (1.f - b1) * gi;
-    const float vi = b2 * v[i] + (1.f - b2) * gi * gi;
-    pi -= step * mi / (sqrtf(vi) / bc2_sqrt + eps);
+  auto upd = [&](float pi, float gi, float& mi, float& vi) {
+    gi *= coef;
+    pi *= decay;
+    mi = b1 * mi + (1.f - b1) * gi;
+    vi = b2 * vi + (1.f - b2) * gi * gi;
+    return pi - step * mi / (sqrtf(vi) / bc2_sqrt + eps);
+  };
+  // 16-byte vectors when every pointer allows it, scalar tail / fallback
+  const bool vec = ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(m) |
+                     reinterpret_cast<uintptr_t>(v)) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 7) == 0;
+  long done = 0;
+  if (vec) {
+    const long nv = n / 4;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < nv; i += (long)gridDim.x * blockDim.x) {
+      float4 pp = reinterpret_cast<const float4*>(p)[i], gg = reinterpret_cast<const float4*>(g)[i];
+      float4 mm = reinterpret_cast<const float4*>(m)[i], vv = reinterpret_cast<const float4*>(v)[i];
+      pp.x = upd(pp.x, gg.x, mm.x, vv.x);
+      pp.y = upd(pp.y, gg.y, mm.y, vv.y);
+      pp.z = upd(pp.z, gg.z, mm.z, vv.z);
+      pp.w = upd(pp.w, gg.w, mm.w, vv.w);
+      reinterpret_cast<float4*>(p)[i] = pp;
+      reinterpret_cast<float4*>(m)[i] = mm;
+      reinterpret_cast<float4*>(v)[i] = vv;
+      uint2 o;
+      o.x = pack_bf16x2(pp.x, pp.y);
+      o.y = pack_bf16x2(pp.z, pp.w);
+      reinterpret_cast<uint2*>(out)[i] = o;
+    }
+    done = nv * 4;
+  }
+  for (long i = done + blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    float mi = m[i], vi = v[i];
+    const float pi = upd(p[i], g[i], mi, vi);
     m[i] = mi;
     v[i] = vi;
     p[i] = pi;

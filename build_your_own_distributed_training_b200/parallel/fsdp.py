@@ -114,7 +114,8 @@ class TorchComm:
 
     def reduce_scatter_mean(self, out_shard: torch.Tensor, full: torch.Tensor, world: int) -> None:
         if self.size == 1:
-            out_shard.copy_(full)
+            if out_shard.data_ptr() != full.data_ptr():
+                out_shard.copy_(full)
         elif full.is_cuda:
             dist.reduce_scatter_tensor(out_shard, full, group=self.group)
         else:
@@ -123,7 +124,8 @@ class TorchComm:
             out_shard.copy_(tmp.chunk(self.size)[self.rank])
         if self.rsize > 1:
             dist.all_reduce(out_shard, group=self.rgroup)
-        out_shard.div_(world)
+        if world != 1:
+            out_shard.div_(world)
 
     def all_reduce_sum(self, t: torch.Tensor, group: dist.ProcessGroup | None) -> None:
         dist.all_reduce(t, group=group)
@@ -234,7 +236,9 @@ class FullyShardedModel(nn.Module):
             u.param_shard.copy_(u.master.to(pdt))
             u.grad = sym(u.numel, torch.float32) if sym else torch.zeros(u.numel, dtype=torch.float32, device=dev)
             u.grad.zero_()
-            u.grad_shard = torch.zeros(u.shard_numel, dtype=torch.float32, device=dev)
+            # unsharded units reduce in place: the gradient shard is the gradient buffer
+            u.grad_shard = u.grad if self.shard_world == 1 else torch.zeros(u.shard_numel, dtype=torch.float32,
+                                                                            device=dev)
         n_slots = 2 if self.cfg.limit_all_gathers else 3
         block_units = self.units[:-1]
         persistent = self.strategy in ("NO_SHARD", "SHARD_GRAD_OP") or self.shard_world == 1

@@ -246,3 +246,32 @@ def test_attention_lse_scale():
     sc = q @ k.transpose(1, 2) / math.sqrt(hd)
     sc = sc.masked_fill(torch.triu(torch.ones(s, s, device=DEV, dtype=torch.bool), 1), float("-inf"))
     assert _rel(lse[0], torch.logsumexp(sc, -1)) < 1e-4
+
+
+@pytest.mark.parametrize("b,s,nq,nkv,hd", [(1, 128, 2, 2, 128), (2, 256, 4, 2, 128), (1, 512, 8, 2, 64),
+                                           (1, 1024, 4, 4, 128), (2, 384, 2, 1, 64)])
+def test_attention_tcgen05_forward(b, s, nq, nkv, hd):
+    qkv = _rand(b * s, (nq + 2 * nkv) * hd)
+    scale = 1 / math.sqrt(hd)
+    o, lse = native().attn_fwd(qkv, b, s, nq, nkv, hd, scale)
+    o_legacy, lse_legacy = native().attn_fwd(qkv, b, s, nq, nkv, hd, scale, legacy=True)
+    ref = _attn_ref(qkv, b, s, nq, nkv, hd)
+    assert _rel(o, ref) < 2e-2
+    assert _rel(o, o_legacy) < 2e-2
+    assert _rel(lse, lse_legacy) < 1e-4
+
+
+@pytest.mark.parametrize("b,s,nq,nkv,hd", [(1, 128, 2, 2, 128), (2, 256, 4, 2, 128), (1, 512, 8, 2, 64),
+                                           (1, 1024, 4, 4, 128)])
+def test_attention_tcgen05_backward(b, s, nq, nkv, hd):
+    qkv = _rand(b * s, (nq + 2 * nkv) * hd)
+    scale = 1 / math.sqrt(hd)
+    o, lse = native().attn_fwd(qkv, b, s, nq, nkv, hd, scale)
+    do = _rand(b * s, nq * hd)
+    d_tc = native().attn_bwd(do, qkv, o, lse, b, s, nq, nkv, hd, scale)
+    d_legacy = native().attn_bwd(do, qkv, o, lse, b, s, nq, nkv, hd, scale, legacy=True)
+    ref_in = qkv.detach().float().requires_grad_()
+    _attn_ref(ref_in, b, s, nq, nkv, hd).backward(do.float())
+    assert _rel(d_tc, ref_in.grad) < 3e-2
+    assert _rel(d_tc, d_legacy) < 2e-2
+    assert torch.equal(d_tc, native().attn_bwd(do, qkv, o, lse, b, s, nq, nkv, hd, scale))
