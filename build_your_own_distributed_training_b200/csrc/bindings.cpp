@@ -21,6 +21,21 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t B, int64_t S, int
 torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, int64_t B, int64_t S,
                        int64_t nq, int64_t nkv, int64_t hd, double scale, bool legacy);
 int64_t device_error();
+void gemm_peer_ar(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool b_mn, c10::optional<torch::Tensor> R,
+                  c10::optional<torch::Tensor> alpha, std::vector<int64_t> bases, int64_t rank, int64_t stage_off,
+                  int64_t flag_off, int64_t epoch, double timeout_s);
+torch::Tensor sym_malloc(int64_t nbytes);
+torch::Tensor ipc_handle(torch::Tensor heap);
+int64_t ipc_open(torch::Tensor handle);
+void ipc_close(int64_t ptr);
+void peer_barrier(std::vector<int64_t> bases, int64_t flag_off, int64_t rank, int64_t epoch, double timeout_s);
+void peer_all_gather(std::vector<int64_t> bases, int64_t src_off, int64_t shard_bytes, torch::Tensor out);
+torch::Tensor peer_reduce_scatter(std::vector<int64_t> bases, int64_t grad_off, int64_t rank, double scale,
+                                  torch::Tensor out);
+void peer_all_reduce_bf16(std::vector<int64_t> bases, int64_t src_off, c10::optional<torch::Tensor> residual,
+                          torch::Tensor out);
+void peer_reduce_rows_bf16(std::vector<int64_t> bases, int64_t src_off, int64_t row0, int64_t cols, torch::Tensor out);
+void wait_flag_probe(torch::Tensor flag, int64_t target, double timeout_s);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels for B200-native 2-D parallel LLaMA training";
@@ -40,4 +55,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd", &attn_bwd, py::arg("dO"), py::arg("qkv"), py::arg("o"), py::arg("lse"), py::arg("B"),
         py::arg("S"), py::arg("nq"), py::arg("nkv"), py::arg("hd"), py::arg("scale"), py::arg("legacy") = false);
   m.def("device_error", &device_error, "read and clear the device error word");
+  m.def("gemm_peer_ar", &gemm_peer_ar, "tcgen05 GEMM fused with an NVLink all-reduce over the peer group");
+  m.def("sym_malloc", &sym_malloc, "raw device allocation for a symmetric heap");
+  m.def("ipc_handle", &ipc_handle);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("peer_barrier", &peer_barrier);
+  m.def("peer_all_gather", &peer_all_gather);
+  m.def("peer_reduce_scatter", &peer_reduce_scatter);
+  m.def("peer_all_reduce_bf16", &peer_all_reduce_bf16);
+  m.def("peer_reduce_rows_bf16", &peer_reduce_rows_bf16);
+  m.def("wait_flag_probe", &wait_flag_probe, "bounded wait on a flag (tests the timeout path)");
 }

@@ -181,6 +181,36 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// ---------------------------------------------------------------- peer memory
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// 16-byte load that bypasses L1 (peer data must not come from a stale L1 line)
+__device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+// Spin until *p >= target (wrap-safe); false after timeout_ns (ERR_PEER_TIMEOUT recorded).
+__device__ __forceinline__ bool wait_flag(const uint32_t* p, uint32_t target, uint64_t timeout_ns, int* err) {
+  if ((int32_t)(ld_acquire_sys(p) - target) >= 0) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    for (int i = 0; i < 32; ++i)
+      if ((int32_t)(ld_acquire_sys(p) - target) >= 0) return true;
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      if (err) atomicExch(err, ERR_PEER_TIMEOUT);
+      return false;
+    }
+    __nanosleep(64);
+  }
+}
+
 }  // namespace dtb
 
 // Host-side argument/CUDA checks that format with snprintf (no iostreams),

@@ -6,14 +6,15 @@
 // three products of a linear layer (forward x.W^T, input grad dy.W, weight
 // grad dy^T.x) all run without transposing anything in memory.
 //
-// CTA = 6 warps, one CTA per SM, grid = min(#tiles, #SMs), static tile stride:
+// CTA = 10 warps, one CTA per SM, grid = min(#tiles, #SMs), static tile stride:
 //   warp 0      TMA producer: one elected thread streams 128x64 A and BNx64 B
 //               tiles (128-byte swizzle) into a STAGES-deep smem ring;
 //   warp 1      owns the TMEM allocation (2 x BN fp32 columns: the accumulator
 //               is double buffered) and one thread issues tcgen05.mma
 //               128xBNx16 instructions; tcgen05.commit releases smem stages
 //               and publishes finished accumulators;
-//   warps 2-5   epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
+//   warps 2-9   epilogue, two warpgroups taking alternate tiles (one per TMEM
+//               accumulator buffer): tcgen05.ld the accumulator (warp w reads TMEM lanes
 //               32*(w%4)..+31 = tile rows), apply the fused epilogue and store,
 //               while the MMA warp already accumulates the next tile into the
 //               other TMEM buffer.
@@ -43,7 +44,10 @@ enum Epi : int {
   EPI_RESIDUAL = 3,
   EPI_ROPE = 4,
   EPI_SWIGLU = 5,
+  EPI_PEER_AR = 6,  // D = sum over the TP group of every rank's tile (+ R), through NVLink peer memory
 };
+
+constexpr int MAX_PEERS = 8;
 
 struct GemmArgs {
   int M, N, K;          // N: output columns (for SwiGLU: F)
@@ -60,6 +64,12 @@ struct GemmArgs {
   int ffn;
   int m_blocks, n_blocks, k_iters, num_tiles;
   int* err;
+  // EPI_PEER_AR: symmetric heaps of the group, staging area and flags inside them
+  uint8_t* peer_base[MAX_PEERS];
+  int peer_n, peer_rank;
+  long stage_off, flag_off;
+  uint32_t epoch;
+  uint64_t timeout_ns;
 };
 
 constexpr int BM = 128;
@@ -234,9 +244,120 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
   }
 }
 
+// ---------------------------------------------------------------- GEMM -> all-reduce
+// Phase 1 (TMEM still held): this thread's row of the tile -> bf16 in the
+// local staging area of the symmetric heap (same [M, N] layout as D).
+template <int BN>
+__device__ __forceinline__ void peer_ar_stage(const GemmArgs& a, uint32_t tbase, int mb, int nb, int quad, int lane) {
+  const int row = mb * BM + quad * 32 + lane;
+  const uint32_t trow = tbase + ((uint32_t)(quad * 32) << 16);
+  const int n0 = nb * BN;
+  __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(a.peer_base[a.peer_rank] + a.stage_off);
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    if (n0 + c >= a.N) break;
+    float v[32];
+    tmem_ld32(trow + c, v);
+    if (row < a.M) {
+      if (a.alpha != nullptr) {
+        const float s = *a.alpha;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] *= s;
+      }
+      store_bf16_32(stage + (long)row * a.ldd + n0 + c, v);
+    }
+  }
+}
+
+// Phase 2: publish this (tile, quadrant) to every peer.  bar.warp.sync orders
+// the other lanes' staging stores before the releasing lane's flag store, and
+// release is cumulative, so one system-scope release per peer suffices.
+__device__ __forceinline__ void peer_ar_publish(const GemmArgs& a, int tile, int quad, int lane) {
+  const long nflags = (long)a.num_tiles * 4;
+  const long f = (long)tile * 4 + quad;
+  __syncwarp();
+  if (lane < a.peer_n)
+    st_release_sys(reinterpret_cast<uint32_t*>(a.peer_base[lane] + a.flag_off) + (long)a.peer_rank * nflags + f,
+                   a.epoch);
+}
+
+// Phase 3 (one tile later, so the flag round trip overlaps the next tile):
+// wait for every peer's copy of the tile, then sum the staged tiles in rank
+// order (+ residual) into D.  All ranks add the same bf16 partials in the same
+// order, so they agree bitwise.
+template <int BN>
+__device__ __forceinline__ bool peer_ar_finish(const GemmArgs& a, int tile, int mb, int nb, int quad, int lane) {
+  const int row = mb * BM + quad * 32 + lane;
+  const int n0 = nb * BN;
+  const long nflags = (long)a.num_tiles * 4;
+  const long f = (long)tile * 4 + quad;
+  const uint32_t* mine = reinterpret_cast<const uint32_t*>(a.peer_base[a.peer_rank] + a.flag_off);
+  bool ok = true;
+  for (int p = 0; p < a.peer_n && ok; ++p) ok = wait_flag(mine + (long)p * nflags + f, a.epoch, a.timeout_ns, a.err);
+  if (!ok) return false;
+  (void)row;
+  // the warp owns rows [row0, row0 + 32); lanes run across the columns so each
+  // load instruction reads one contiguous 512-byte row segment from a peer,
+  // and four rows are in flight per peer
+  const int row0 = mb * BM + quad * 32;
+  const int cols = min(BN, a.N - n0);
+  const int c = lane * 8;
+  if (c >= cols) return true;
+  constexpr int RU = 4;
+#pragma unroll 1
+  for (int r = 0; r < 32; r += RU) {
+    float acc[RU][8];
+#pragma unroll
+    for (int i = 0; i < RU; ++i)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[i][k] = 0.f;
+    for (int p = 0; p < a.peer_n; ++p) {
+      uint4 v[RU];
+#pragma unroll
+      for (int i = 0; i < RU; ++i) {
+        const int rr = row0 + r + i;
+        v[i] = rr < a.M ? ld_cg_v4(a.peer_base[p] + a.stage_off + ((long)rr * a.ldd + n0 + c) * 2)
+                        : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int i = 0; i < RU; ++i) {
+        const uint32_t* u = &v[i].x;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 t = unpack_bf16x2(u[k]);
+          acc[i][2 * k] += t.x;
+          acc[i][2 * k + 1] += t.y;
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < RU; ++i) {
+      const int rr = row0 + r + i;
+      if (rr >= a.M) continue;
+      if (a.R != nullptr) {
+        const uint4 q = *reinterpret_cast<const uint4*>(a.R + (long)rr * a.ldr + n0 + c);
+        const uint32_t* u = &q.x;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 t = unpack_bf16x2(u[k]);
+          acc[i][2 * k] += t.x;
+          acc[i][2 * k + 1] += t.y;
+        }
+      }
+      uint4 o;
+      o.x = pack_bf16x2(acc[i][0], acc[i][1]);
+      o.y = pack_bf16x2(acc[i][2], acc[i][3]);
+      o.z = pack_bf16x2(acc[i][4], acc[i][5]);
+      o.w = pack_bf16x2(acc[i][6], acc[i][7]);
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.D) + (long)rr * a.ldd + n0 + c) = o;
+    }
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------- kernel
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const GemmArgs args) {
   using L = SmemLayout<BN, STAGES>;
@@ -360,10 +481,16 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
+    // two epilogue warpgroups (warps 2-5 and 6-9): group g drains the tiles
+    // that land in TMEM buffer g, so each group has two tiles of time for its
+    // stores and twice as many memory requests are in flight per SM
     const int quad = warp & 3;
+    const int wg = (warp - 2) >> 2;
     int t = 0;
+    int pend_tile = -1, pend_mb = 0, pend_nb = 0;  // EPI_PEER_AR: tile published, not yet reduced
     for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++t) {
       const int acc = t & 1;
+      if (acc != wg) continue;
       const uint32_t acc_phase = (t >> 1) & 1;
       int mb, nb;
       tile_coords(tile, args.m_blocks, args.n_blocks, mb, nb);
@@ -372,9 +499,27 @@ __global__ void __launch_bounds__(192, 1)
         break;
       }
       tc_fence_after();
-      epilogue_tile<BN, EPI>(args, tmem_base + acc * BN, mb, nb, quad, lane);
-      tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);
+      if constexpr (EPI == EPI_PEER_AR) {
+        peer_ar_stage<BN>(args, tmem_base + acc * BN, mb, nb, quad, lane);
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);  // the MMA warp may reuse this buffer while we exchange
+        peer_ar_publish(args, tile, quad, lane);
+        if (pend_tile >= 0 && !peer_ar_finish<BN>(args, pend_tile, pend_mb, pend_nb, quad, lane)) {
+          *abort_flag = 1;
+          pend_tile = -1;
+          break;
+        }
+        pend_tile = tile;
+        pend_mb = mb;
+        pend_nb = nb;
+      } else {
+        epilogue_tile<BN, EPI>(args, tmem_base + acc * BN, mb, nb, quad, lane);
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);
+      }
+    }
+    if constexpr (EPI == EPI_PEER_AR) {
+      if (pend_tile >= 0 && !peer_ar_finish<BN>(args, pend_tile, pend_mb, pend_nb, quad, lane)) *abort_flag = 1;
     }
   }
   tc_fence_before();
@@ -443,7 +588,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cu
   }
   const int grid = std::min(g.num_tiles, num_sms());
   if (grid == 0) return;
-  kern<<<grid, 192, L::TOTAL, st>>>(ta, tb, g);
+  kern<<<grid, 320, L::TOTAL, st>>>(ta, tb, g);
   DTB_LAUNCH_CHECK();
 }
 
@@ -463,6 +608,9 @@ static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, 
     case EPI_SWIGLU:
       if constexpr (!A_MN && !B_MN && BN == 256) { launch<BN, ST, A_MN, B_MN, EPI_SWIGLU>(ta, tb, g, st); break; }
       TORCH_CHECK(false, "swiglu epilogue needs K-major operands and BN=256");
+    case EPI_PEER_AR:
+      if constexpr (!A_MN) { launch<BN, ST, A_MN, B_MN, EPI_PEER_AR>(ta, tb, g, st); break; }
+      TORCH_CHECK(false, "peer all-reduce epilogue needs a K-major A operand");
     default: DTB_CHECK(false, "unknown epilogue %d", epi);
   }
 }
@@ -472,10 +620,18 @@ static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, 
 // Python entry: see ops/gemm.py for the operand conventions.
 //   A: [M,K] (a_mn=false) or [K,M] (a_mn=true); B: [N,K] or [K,N]; D: [M,N]
 //   (SwiGLU: B = [2F,K], D = [M,F], D2 = [M,2F]; p0 = F).
-void gemm_entry(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_mn, bool b_mn, int64_t epi,
-                c10::optional<torch::Tensor> R, c10::optional<torch::Tensor> alpha,
-                c10::optional<torch::Tensor> cos_t, c10::optional<torch::Tensor> sin_t,
-                c10::optional<torch::Tensor> D2, int64_t p0, int64_t p1) {
+struct PeerCfg {
+  std::vector<int64_t> bases;
+  int rank;
+  long stage_off, flag_off;
+  uint32_t epoch;
+  double timeout_s;
+};
+
+static void gemm_impl(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_mn, bool b_mn, int64_t epi,
+                      c10::optional<torch::Tensor> R, c10::optional<torch::Tensor> alpha,
+                      c10::optional<torch::Tensor> cos_t, c10::optional<torch::Tensor> sin_t,
+                      c10::optional<torch::Tensor> D2, int64_t p0, int64_t p1, const PeerCfg* peer) {
   using namespace dtb;
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && D.is_cuda(), "gemm: CUDA tensors expected");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm: bf16 operands expected");
@@ -495,11 +651,25 @@ void gemm_entry(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_mn, bo
   g.D = D.data_ptr();
   g.ldd = D.stride(0);
   g.err = dtb_error_word();
+  if (peer != nullptr) {
+    DTB_CHECK(epi == EPI_PEER_AR && peer->bases.size() >= 1 && peer->bases.size() <= (size_t)MAX_PEERS,
+              "peer GEMM: bad group");
+    for (size_t i = 0; i < peer->bases.size(); ++i) g.peer_base[i] = reinterpret_cast<uint8_t*>(peer->bases[i]);
+    g.peer_n = (int)peer->bases.size();
+    g.peer_rank = peer->rank;
+    g.stage_off = peer->stage_off;
+    g.flag_off = peer->flag_off;
+    g.epoch = peer->epoch;
+    g.timeout_ns = (uint64_t)(peer->timeout_s * 1e9);
+    DTB_CHECK(peer->stage_off % 16 == 0 && D.size(1) % 8 == 0, "peer GEMM: staging must be 16-byte aligned");
+  } else {
+    DTB_CHECK(epi != EPI_PEER_AR, "peer all-reduce epilogue needs a peer group");
+  }
   const bool f32out = D.scalar_type() == at::kFloat;
   int e = (int)epi;
   if (e == EPI_STORE_BF16 && f32out) e = EPI_STORE_F32;
   if (e == EPI_ACC_F32) TORCH_CHECK(f32out, "gemm: accumulate epilogue needs an fp32 output");
-  if (e == EPI_STORE_BF16 || e == EPI_RESIDUAL || e == EPI_ROPE || e == EPI_SWIGLU)
+  if (e == EPI_STORE_BF16 || e == EPI_RESIDUAL || e == EPI_ROPE || e == EPI_SWIGLU || e == EPI_PEER_AR)
     TORCH_CHECK(D.scalar_type() == at::kBFloat16, "gemm: bf16 output expected");
   TORCH_CHECK(D.stride(1) == 1 && D.stride(0) % 8 == 0, "gemm: output rows must be contiguous and 16B aligned");
   if (alpha.has_value()) {
@@ -507,6 +677,11 @@ void gemm_entry(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_mn, bo
     g.alpha = alpha->data_ptr<float>();
   }
   int BN = NB > 128 ? 256 : 128;
+  if (e == EPI_PEER_AR && R.has_value()) {
+    DTB_CHECK(R->scalar_type() == at::kBFloat16 && R->stride(1) == 1, "gemm: bad residual");
+    g.R = reinterpret_cast<const __nv_bfloat16*>(R->data_ptr());
+    g.ldr = R->stride(0);
+  }
   if (e == EPI_RESIDUAL) {
     TORCH_CHECK(R.has_value() && R->scalar_type() == at::kBFloat16 && R->stride(1) == 1, "gemm: bad residual");
     g.R = reinterpret_cast<const __nv_bfloat16*>(R->data_ptr());
@@ -556,4 +731,21 @@ void gemm_entry(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_mn, bo
     else if (a_mn && b_mn) dispatch_epi<128, true, true>(e, ta, tb, g, st);
     else TORCH_CHECK(false, "gemm: layout (MN, K) not built");
   }
+}
+
+void gemm_entry(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_mn, bool b_mn, int64_t epi,
+                c10::optional<torch::Tensor> R, c10::optional<torch::Tensor> alpha,
+                c10::optional<torch::Tensor> cos_t, c10::optional<torch::Tensor> sin_t,
+                c10::optional<torch::Tensor> D2, int64_t p0, int64_t p1) {
+  gemm_impl(A, B, D, a_mn, b_mn, epi, R, alpha, cos_t, sin_t, D2, p0, p1, nullptr);
+}
+
+// D = sum over the peer group of (A x B) (+ R): the GEMM fused with an
+// all-reduce through the symmetric heaps (staging at stage_off, flags at
+// flag_off, both inside every rank's heap; epoch increases by one per call).
+void gemm_peer_ar(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool b_mn, c10::optional<torch::Tensor> R,
+                  c10::optional<torch::Tensor> alpha, std::vector<int64_t> bases, int64_t rank, int64_t stage_off,
+                  int64_t flag_off, int64_t epoch, double timeout_s) {
+  PeerCfg pc{bases, (int)rank, (long)stage_off, (long)flag_off, (uint32_t)epoch, timeout_s};
+  gemm_impl(A, B, D, false, b_mn, dtb::EPI_PEER_AR, R, alpha, c10::nullopt, c10::nullopt, c10::nullopt, 0, 0, &pc);
 }

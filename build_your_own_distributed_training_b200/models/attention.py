@@ -40,7 +40,7 @@ class Attention(nn.Module):
         """``x``: ``[b, s, d]`` (or local ``[tokens, d]`` under sequence parallelism)."""
         out_shape = x.shape if residual is None else residual.shape
         seqlen = cos.shape[0]
-        x2 = tpar.column_input(x.reshape(-1, x.shape[-1]), self.tp)
+        x2, grad_comm = tpar.column_input_fused(x.reshape(-1, x.shape[-1]), self.tp)
         hd = self.head_dim
         nq, nkv = self.wq.weight.shape[0] // hd, self.wk.weight.shape[0] // hd
         if self.wq.bias is not None:
@@ -52,7 +52,7 @@ class Attention(nn.Module):
             rope_forward(qkv, cos, sin, (nq + nkv) * hd, hd, seqlen)
         else:
             w, mg = fused_rows([self.wq.weight, self.wk.weight, self.wv.weight])
-            qkv = linear_qkv_rope(x2, w, cos, sin, nq, nkv, hd, seqlen, main_grad=mg)
+            qkv = linear_qkv_rope(x2, w, cos, sin, nq, nkv, hd, seqlen, main_grad=mg, grad_comm=grad_comm)
         o = causal_attention(qkv, x2.shape[0] // seqlen, seqlen, nq, nkv, hd,
                              self.dropout_p if self.training else 0.0)
         r2 = residual.reshape(-1, residual.shape[-1]) if residual is not None else None

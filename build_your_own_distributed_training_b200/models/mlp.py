@@ -29,7 +29,7 @@ class SwiGLUMLP(nn.Module):
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
         out_shape = x.shape if residual is None else residual.shape
-        x2 = tpar.column_input(x.reshape(-1, x.shape[-1]), self.tp)
+        x2, grad_comm = tpar.column_input_fused(x.reshape(-1, x.shape[-1]), self.tp)
         ffn = self.gate_proj.weight.shape[0]
         if self.gate_proj.bias is not None:
             g = F.linear(x2, self.gate_proj.weight.to(x2.dtype), self.gate_proj.bias.to(x2.dtype))
@@ -37,7 +37,7 @@ class SwiGLUMLP(nn.Module):
             act = F.silu(g) * u
         else:
             w, mg = fused_rows([self.gate_proj.weight, self.up_proj.weight])
-            act = linear_swiglu(x2, w, ffn, main_grad=mg)
+            act = linear_swiglu(x2, w, ffn, main_grad=mg, grad_comm=grad_comm)
         r2 = residual.reshape(-1, residual.shape[-1]) if residual is not None else None
         y = tpar.row_output_linear(act, self.down_proj.weight, r2, self.tp,
                                    main_grad=main_grad_of(self.down_proj.weight),

@@ -28,6 +28,12 @@ def _flat(x: torch.Tensor) -> torch.Tensor:
     return x.reshape(-1, x.shape[-1])
 
 
+def _input_grad(dy2: torch.Tensor, weight: torch.Tensor, grad_comm) -> torch.Tensor:
+    if grad_comm is not None:
+        return grad_comm.gemm_all_reduce_dgrad(dy2, weight)
+    return gemm.mm_nn(dy2, weight)
+
+
 def _weight_grad(dy2: torch.Tensor, x2: torch.Tensor, weight: torch.Tensor,
                  main_grad: torch.Tensor | None) -> torch.Tensor | None:
     if main_grad is not None:
@@ -72,7 +78,7 @@ def linear(x: torch.Tensor, weight: torch.Tensor, *, bias: torch.Tensor | None =
 
 class _QKVRopeFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, weight, cos, sin, rope_cols, head_dim, seqlen, main_grad):  # type: ignore[override]
+    def forward(ctx, x, weight, cos, sin, rope_cols, head_dim, seqlen, main_grad, grad_comm):  # type: ignore[override]
         x2 = _flat(x)
         if x2.is_cuda:
             y = gemm.mm_nt_rope(x2, weight, cos, sin, rope_cols, head_dim, seqlen)
@@ -82,6 +88,7 @@ class _QKVRopeFn(torch.autograd.Function):
         ctx.save_for_backward(x2, weight, cos, sin)
         ctx.cfg = (rope_cols, head_dim, seqlen)
         ctx.main_grad = main_grad
+        ctx.grad_comm = grad_comm
         return y.view(*x.shape[:-1], weight.shape[0])
 
     @staticmethod
@@ -91,14 +98,14 @@ class _QKVRopeFn(torch.autograd.Function):
         d = _flat(dy).contiguous().clone()
         rope_backward_(d, cos, sin, rope_cols, head_dim, seqlen)
         wc = w if d.is_cuda else w.to(d.dtype)
-        dx = gemm.mm_nn(d, wc).view(*dy.shape[:-1], w.shape[1])
+        dx = _input_grad(d, wc, ctx.grad_comm).view(*dy.shape[:-1], w.shape[1])
         dw = _weight_grad(d, x2, w, ctx.main_grad)
-        return dx, dw, None, None, None, None, None, None
+        return dx, dw, None, None, None, None, None, None, None
 
 
 def linear_qkv_rope(x: torch.Tensor, weight: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                     n_q_heads: int, n_kv_heads: int, head_dim: int, seqlen: int, *,
-                    main_grad: torch.Tensor | None = None) -> torch.Tensor:
+                    main_grad: torch.Tensor | None = None, grad_comm=None) -> torch.Tensor:
     """Packed ``[q | k | v]`` projection with RoPE applied to ``q`` and ``k``.
 
     ``weight`` is ``[Wq; Wk; Wv]`` (``[(nq + 2 nkv) * hd, d]``); ``x`` is
@@ -106,7 +113,7 @@ def linear_qkv_rope(x: torch.Tensor, weight: torch.Tensor, cos: torch.Tensor, si
     """
     rope_cols = (n_q_heads + n_kv_heads) * head_dim
     return _QKVRopeFn.apply(x.contiguous(), weight, cos, sin, rope_cols, head_dim, seqlen,
-                            main_grad)
+                            main_grad, grad_comm)
 
 
 def swiglu_reference(gu: torch.Tensor, ffn: int) -> torch.Tensor:
@@ -132,7 +139,7 @@ def swiglu_backward(dact: torch.Tensor, gu: torch.Tensor, ffn: int) -> torch.Ten
 
 class _SwiGLUFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, weight, ffn, main_grad):  # type: ignore[override]
+    def forward(ctx, x, weight, ffn, main_grad, grad_comm):  # type: ignore[override]
         x2 = _flat(x)
         if x2.is_cuda and ffn % 128 == 0:
             act, gu = gemm.mm_nt_swiglu(x2, weight, ffn)
@@ -144,6 +151,7 @@ class _SwiGLUFn(torch.autograd.Function):
         ctx.save_for_backward(x2, weight, gu)
         ctx.ffn = ffn
         ctx.main_grad = main_grad
+        ctx.grad_comm = grad_comm
         return act.view(*x.shape[:-1], ffn)
 
     @staticmethod
@@ -151,12 +159,16 @@ class _SwiGLUFn(torch.autograd.Function):
         x2, w, gu = ctx.saved_tensors
         dgu = swiglu_backward(_flat(dact), gu, ctx.ffn)
         wc = w if dgu.is_cuda else w.to(dgu.dtype)
-        dx = gemm.mm_nn(dgu, wc).view(*dact.shape[:-1], w.shape[1])
+        dx = _input_grad(dgu, wc, ctx.grad_comm).view(*dact.shape[:-1], w.shape[1])
         dw = _weight_grad(dgu, x2, w, ctx.main_grad)
-        return dx, dw, None, None
+        return dx, dw, None, None, None
 
 
 def linear_swiglu(x: torch.Tensor, weight: torch.Tensor, ffn: int, *,
-                  main_grad: torch.Tensor | None = None) -> torch.Tensor:
-    """``silu(x W_g^T) * (x W_u^T)`` with ``weight = [W_g; W_u]`` (``[2F, d]``)."""
-    return _SwiGLUFn.apply(x.contiguous(), weight, ffn, main_grad)
+                  main_grad: torch.Tensor | None = None, grad_comm=None) -> torch.Tensor:
+    """``silu(x W_g^T) * (x W_u^T)`` with ``weight = [W_g; W_u]`` (``[2F, d]``).
+
+    ``grad_comm``: a TP transport whose ``gemm_all_reduce_dgrad`` computes the
+    input gradient and its TP all-reduce in one kernel (column-parallel use).
+    """
+    return _SwiGLUFn.apply(x.contiguous(), weight, ffn, main_grad, grad_comm)

@@ -225,16 +225,26 @@ class FullyShardedModel(nn.Module):
     def _alloc(self) -> None:
         dev = self.device
         pdt = self.policy.param_dtype
-        sym = getattr(self.comm, "alloc", None)
-        for u in self.units:
+        # buffers peers read (parameter shards, gradient buffers) go into the
+        # transport's symmetric heap when it has one
+        heap_views: list[torch.Tensor] = []
+        if hasattr(self.comm, "alloc_many"):
+            specs = []
+            for u in self.units:
+                specs += [(u.shard_numel, pdt), (u.numel, torch.float32)]
+            heap_views = self.comm.alloc_many(specs)
+        for ui, u in enumerate(self.units):
             full = torch.zeros(u.numel, dtype=torch.float32)
             for e in u.entries:
                 full[e.offset:e.offset + e.numel] = e.param.detach().reshape(-1).float().cpu()
             lo, hi = u.shard_range(self.shard_rank)
             u.master = full[lo:hi].clone().to(dev)
-            u.param_shard = sym(u.shard_numel, pdt) if sym else torch.empty(u.shard_numel, dtype=pdt, device=dev)
+            if heap_views:
+                u.param_shard, u.grad = heap_views[2 * ui], heap_views[2 * ui + 1]
+            else:
+                u.param_shard = torch.empty(u.shard_numel, dtype=pdt, device=dev)
+                u.grad = torch.empty(u.numel, dtype=torch.float32, device=dev)
             u.param_shard.copy_(u.master.to(pdt))
-            u.grad = sym(u.numel, torch.float32) if sym else torch.zeros(u.numel, dtype=torch.float32, device=dev)
             u.grad.zero_()
             # unsharded units reduce in place: the gradient shard is the gradient buffer
             u.grad_shard = u.grad if self.shard_world == 1 else torch.zeros(u.shard_numel, dtype=torch.float32,

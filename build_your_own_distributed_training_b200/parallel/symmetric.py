@@ -1,9 +1,321 @@
-"""Placeholder: filled in with the NVLink peer-memory transport."""
+"""NVLink transport: symmetric heaps and the collectives built on them.
+
+Every rank of a group allocates one device buffer of the same size (a raw
+``cudaMalloc``), exports it with a CUDA IPC handle, and maps every peer's
+buffer, so each rank holds device pointers to all heaps of its group.  On one
+NVSwitch node every GPU reaches every peer at full NVLink bandwidth, so the
+collectives are single-step pulls run by this package's kernels
+(``csrc/comm.cu``, ``csrc/gemm.cu``):
+
+* :class:`PeerComm` - the ZeRO engine's transport over the dp group: the bf16
+  parameter shards and the fp32 gradient buffers live in the heap; the
+  all-gather pulls peers' shards, the reduce-scatter pulls this rank's slice
+  of every peer's gradients and sums them in rank order with the 1/dp scale
+  fused (deterministic, identical on every run);
+* :class:`TPComm` - tensor parallelism: the row-parallel GEMM fused with its
+  all-reduce (tiles are exchanged through the heap as the GEMM produces them,
+  summed in rank order, residual added in the same epilogue), and the
+  all-reduce / token all-gather / token reduce-scatter used elsewhere.
+
+Synchronisation is by flags in the heaps (epochs, release/acquire at system
+scope) with bounded waits: a peer that never arrives makes the kernel record
+an error in the device error word and return, and the host raises
+:class:`CollectiveTimeoutError` at the next step boundary.  ``torch.distributed``
+is used only to exchange the IPC handles and for rare scalar reductions.
+"""
+
+from __future__ import annotations
+
+import os
+from typing import Any
+
+import torch
+import torch.distributed as dist
+
+from ..ops._ext import native
+
+TIMEOUT_S = float(os.environ.get("DTB_PEER_TIMEOUT_S", "10"))
+_ALIGN = 256
+_HEAPS: list["SymmetricHeap"] = []
+
+
+class CollectiveTimeoutError(RuntimeError):
+    """A peer-memory wait ran out: a peer died or stopped issuing collectives."""
+
+
+def _align(n: int, a: int = _ALIGN) -> int:
+    return -(-n // a) * a
+
+
+class SymmetricHeap:
+    """One same-sized device buffer per rank of ``group``, mapped into every rank."""
+
+    def __init__(self, group: dist.ProcessGroup, nbytes: int, device: torch.device) -> None:
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.size = dist.get_world_size(group)
+        self.nbytes = _align(nbytes, 1 << 20)
+        with torch.cuda.device(device):
+            self.local = native().sym_malloc(self.nbytes)
+        handle = native().ipc_handle(self.local).tolist()
+        handles: list[Any] = [None] * self.size
+        dist.all_gather_object(handles, handle, group=group)
+        self.bases: list[int] = []
+        self._opened: list[int] = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.bases.append(self.local.data_ptr())
+            else:
+                ptr = native().ipc_open(torch.tensor(h, dtype=torch.uint8))
+                self.bases.append(ptr)
+                self._opened.append(ptr)
+        self._top = 0
+        _HEAPS.append(self)
+
+    def alloc(self, nbytes: int) -> int:
+        off = self._top
+        self._top = _align(off + nbytes)
+        if self._top > self.nbytes:
+            raise MemoryError(f"symmetric heap exhausted ({self._top} > {self.nbytes} bytes)")
+        return off
+
+    def view(self, off: int, numel: int, dtype: torch.dtype) -> torch.Tensor:
+        nb = numel * torch.empty((), dtype=dtype).element_size()
+        return self.local[off:off + nb].view(dtype)
+
+    def offset_of(self, t: torch.Tensor) -> int:
+        off = t.data_ptr() - self.local.data_ptr()
+        if not 0 <= off < self.nbytes:
+            raise ValueError("tensor is not inside this symmetric heap")
+        return off
+
+    def close(self) -> None:
+        for p in self._opened:
+            try:
+                native().ipc_close(p)
+            except RuntimeError:
+                pass
+        self._opened.clear()
 
 
 def release_all() -> None:
-    pass
+    """Unmap every peer heap (call before the process group is destroyed)."""
+    if torch.cuda.is_available() and _HEAPS:
+        torch.cuda.synchronize()
+    for h in _HEAPS:
+        h.close()
+    _HEAPS.clear()
 
 
-def build_comms(ctx, config):
-    return None, None
+def check_device_errors() -> None:
+    """Raise if a kernel recorded a timeout or bad argument since the last check."""
+    err = native().device_error()
+    if err == 2:
+        raise CollectiveTimeoutError(
+            "a peer-memory wait timed out (a peer stopped participating); see DTB_PEER_TIMEOUT_S")
+    if err:
+        raise RuntimeError(f"device error word set: {err}")
+
+
+class _Barrier:
+    """Device barrier over a heap's group on one flag channel."""
+
+    def __init__(self, heap: SymmetricHeap) -> None:
+        self.heap = heap
+        self.off = heap.alloc(128)
+        self.epoch = 0
+
+    def __call__(self) -> None:
+        self.epoch += 1
+        native().peer_barrier(self.heap.bases, self.off, self.heap.rank, self.epoch, TIMEOUT_S)
+
+
+# ----------------------------------------------------------------------------- ZeRO (dp)
+class PeerComm:
+    """The sharding engine's transport over the dp group (see module docstring)."""
+
+    name = "peer"
+
+    def __init__(self, group: dist.ProcessGroup, device: torch.device) -> None:
+        self.group = group
+        self.size = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.rgroup, self.rsize = None, 1
+        self.device = device
+        self.heap: SymmetricHeap | None = None
+
+    # the engine asks for all heap-resident buffers at once
+    def alloc_many(self, specs: list[tuple[int, torch.dtype]]) -> list[torch.Tensor]:
+        sizes = [_align(n * torch.empty((), dtype=d).element_size()) for n, d in specs]
+        self.heap = SymmetricHeap(self.group, sum(sizes) + 64 * 1024, self.device)
+        self._step_barrier = _Barrier(self.heap)
+        self._rs_barrier = _Barrier(self.heap)
+        out = []
+        for (n, d), nb in zip(specs, sizes):
+            out.append(self.heap.view(self.heap.alloc(nb), n, d))
+        return out
+
+    def barrier(self) -> None:
+        if self.heap is not None:
+            self._step_barrier()
+
+    def all_gather(self, out_full: torch.Tensor, shard: torch.Tensor) -> None:
+        assert self.heap is not None
+        nbytes = shard.numel() * shard.element_size()
+        native().peer_all_gather(self.heap.bases, self.heap.offset_of(shard), nbytes, out_full)
+
+    def reduce_scatter_mean(self, out_shard: torch.Tensor, full: torch.Tensor, world: int) -> torch.Tensor:
+        assert self.heap is not None
+        self._rs_barrier()  # every rank finished accumulating this unit's gradients
+        return native().peer_reduce_scatter(self.heap.bases, self.heap.offset_of(full), self.rank, 1.0 / world,
+                                            out_shard)
+
+    def all_reduce_sum(self, t: torch.Tensor, group: dist.ProcessGroup | None) -> None:
+        dist.all_reduce(t, group=group)
+
+
+# ----------------------------------------------------------------------------- TP
+class _RowParallelAR(torch.autograd.Function):
+    """``y = all_reduce(x @ W^T) + residual`` with the all-reduce inside the GEMM."""
+
+    @staticmethod
+    def forward(ctx, x2, weight, residual, main_grad, comm):  # type: ignore[override]
+        out = comm.gemm_all_reduce(x2, weight, residual)
+        ctx.save_for_backward(x2, weight)
+        ctx.main_grad = main_grad
+        ctx.has_res = residual is not None
+        return out
+
+    @staticmethod
+    def backward(ctx, dy):  # type: ignore[override]
+        from ..ops import gemm
+        x2, w = ctx.saved_tensors
+        dy = dy.contiguous()
+        dx = gemm.mm_nn(dy, w)  # the input is TP-sharded: no reduction needed
+        if ctx.main_grad is not None:
+            gemm.mm_tn_acc(dy, x2, ctx.main_grad.view(w.shape))
+            dw = None
+        else:
+            dw = gemm.mm_tn(dy, x2).to(w.dtype) if w.requires_grad else None
+        return dx, dw, (dy if ctx.has_res else None), None, None
+
+
+class TPComm:
+    """Tensor-parallel collectives over NVLink for one TP group."""
+
+    def __init__(self, group: dist.ProcessGroup, device: torch.device, max_tokens: int, width: int) -> None:
+        self.group = group
+        self.size = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.max_tokens, self.width = max_tokens, width
+        self.max_elems = max_tokens * width
+        tiles = (-(-max_tokens // 128)) * (-(-width // 128))
+        self.flag_bytes = _align(tiles * 4 * self.size * 4)
+        slot = _align(self.max_elems * 2)
+        self.heap = SymmetricHeap(group, 2 * slot + self.flag_bytes + 64 * 1024, device)
+        self.slots = [self.heap.alloc(slot), self.heap.alloc(slot)]
+        self.flag_off = self.heap.alloc(self.flag_bytes)
+        self.barrier = _Barrier(self.heap)
+        self.calls = 0
+
+    def _slot(self) -> int:
+        self.calls += 1
+        return self.slots[self.calls % 2]
+
+    def _staging(self, off: int, shape: tuple[int, ...]) -> torch.Tensor:
+        n = 1
+        for s in shape:
+            n *= s
+        if n > self.max_elems:
+            raise ValueError(f"TP staging holds {self.max_elems} elements, {n} requested")
+        return self.heap.view(off, n, torch.bfloat16).view(shape)
+
+    # fused GEMM -> all-reduce (+ residual)
+    def gemm_all_reduce(self, x2: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None) -> torch.Tensor:
+        M, N = x2.shape[0], w.shape[0]
+        if M > self.max_tokens or N > self.width:
+            raise ValueError(f"row-parallel output [{M}, {N}] exceeds the TP staging area "
+                             f"[{self.max_tokens}, {self.width}]")
+        out = torch.empty(M, N, device=x2.device, dtype=torch.bfloat16)
+        off = self._slot()
+        native().gemm_peer_ar(x2, w, out, False, residual, None, self.heap.bases, self.rank, off, self.flag_off,
+                              self.calls, TIMEOUT_S)
+        return out
+
+    # fused input-gradient GEMM -> all-reduce of a column-parallel layer: dy @ W, summed over TP
+    def gemm_all_reduce_dgrad(self, dy: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        M, K = dy.shape[0], w.shape[1]
+        if M > self.max_tokens or K > self.width:
+            raise ValueError(f"input gradient [{M}, {K}] exceeds the TP staging area "
+                             f"[{self.max_tokens}, {self.width}]")
+        out = torch.empty(M, K, device=dy.device, dtype=torch.bfloat16)
+        off = self._slot()
+        native().gemm_peer_ar(dy.contiguous(), w, out, True, None, None, self.heap.bases, self.rank, off,
+                              self.flag_off, self.calls, TIMEOUT_S)
+        return out
+
+    def row_parallel_linear(self, x2, weight, residual, main_grad):
+        from .tensor_parallel import _SeqReduceScatter, TPInfo  # noqa: F401
+        if self._sequence_parallel:
+            from ..ops.linear import linear
+            y = linear(x2, weight, main_grad=main_grad)
+            y = _SeqReduceScatterPeer.apply(y, self)
+            return y + residual if residual is not None else y
+        return _RowParallelAR.apply(x2.contiguous(), weight, residual, main_grad, self)
+
+    _sequence_parallel = False
+
+    # standalone collectives on bf16 activations
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        x = x.contiguous()
+        off = self._slot()
+        self._staging(off, tuple(x.shape)).copy_(x)
+        self.barrier()
+        out = torch.empty_like(x)
+        native().peer_all_reduce_bf16(self.heap.bases, off, None, out)
+        return out
+
+    def all_gather_rows(self, x: torch.Tensor) -> torch.Tensor:
+        x = x.contiguous()
+        off = self._slot()
+        self._staging(off, tuple(x.shape)).copy_(x)
+        self.barrier()
+        out = torch.empty((x.shape[0] * self.size,) + tuple(x.shape[1:]), device=x.device, dtype=x.dtype)
+        native().peer_all_gather(self.heap.bases, off, x.numel() * x.element_size(), out)
+        return out
+
+    def reduce_scatter_rows(self, x: torch.Tensor) -> torch.Tensor:
+        x = x.contiguous()
+        rows = x.shape[0] // self.size
+        cols = x.numel() // x.shape[0]
+        off = self._slot()
+        self._staging(off, tuple(x.shape)).copy_(x)
+        self.barrier()
+        out = torch.empty((rows,) + tuple(x.shape[1:]), device=x.device, dtype=x.dtype)
+        native().peer_reduce_rows_bf16(self.heap.bases, off, self.rank * rows, cols, out)
+        return out
+
+
+class _SeqReduceScatterPeer(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, comm):  # type: ignore[override]
+        ctx.comm = comm
+        return comm.reduce_scatter_rows(x)
+
+    @staticmethod
+    def backward(ctx, g):  # type: ignore[override]
+        return ctx.comm.all_gather_rows(g.contiguous()), None
+
+
+def build_comms(ctx: Any, config: Any) -> tuple[TPComm | None, PeerComm | None]:
+    """Transports for this rank: ``(tp_comm, dp_comm)`` (``None`` for size-1 groups)."""
+    dev = ctx.device
+    tp = dp = None
+    if ctx.dims.tp_size > 1:
+        tokens = config.data.micro_batch_size * config.data.seq_len
+        tp = TPComm(ctx.tp_group, dev, tokens, config.model.d_model)
+        tp._sequence_parallel = bool(config.parallel.sequence_parallel)
+    if ctx.dims.dp_size > 1 and config.parallel.sharding_strategy in ("FULL_SHARD", "SHARD_GRAD_OP") \
+            and ctx.dims.dp_size <= 8:
+        dp = PeerComm(ctx.dp_group, dev)
+    return tp, dp

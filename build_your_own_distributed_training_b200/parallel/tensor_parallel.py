@@ -264,6 +264,16 @@ def sequence_slice(t: torch.Tensor, tp: TPInfo | None) -> torch.Tensor:
     return t[tp.rank * rows:(tp.rank + 1) * rows]
 
 
+def column_input_fused(x2: torch.Tensor, tp: TPInfo | None) -> tuple[torch.Tensor, Any]:
+    """Like :func:`column_input`, but when the NVLink transport can fuse the
+    input-gradient all-reduce into the column-parallel layer's dgrad GEMM,
+    return ``(x2, transport)`` for the layer to do so (no separate f-op)."""
+    if (tp is not None and tp.size > 1 and tp.fused and tp.comm is not None and x2.is_cuda
+            and not tp.sequence_parallel):
+        return x2, tp.comm
+    return column_input(x2, tp), None
+
+
 def column_input(x2: torch.Tensor, tp: TPInfo | None) -> torch.Tensor:
     """Input of a column-parallel GEMM: f operator, or token all-gather under SP."""
     if tp is None or tp.size == 1:

@@ -92,6 +92,9 @@ def train_step(model: nn.Module, micro_batches: Sequence[Batch], optimizer: torc
             dist.all_reduce(loss_t, group=ctx.dp_group)
             loss_t /= ctx.dims.dp_size
         host = torch.stack([loss_t[0], norm, state[1]]).cpu()  # the one host sync
+        if device.type == "cuda":
+            from ..parallel.symmetric import check_device_errors
+            check_device_errors()  # bounded peer waits that ran out raise here
         loss_value, grad_norm, finite = float(host[0]), float(host[1]), bool(host[2] > 0)
         if not finite:
             raise GradNotFiniteError(
