@@ -50,6 +50,7 @@ import torch.distributed as dist
 import torch.nn as nn
 
 from ..config import ParallelConfig
+from ..observability import nvtx
 from ..utils.dtype import build_mixed_precision
 from .tensor_parallel import tp_param_kind
 
@@ -283,6 +284,7 @@ class FullyShardedModel(nn.Module):
     def _make_pre_fwd(self, bi: int):
         def hook(_mod, args):
             in_bwd = _in_backward()
+            nvtx.push(f"block{bi}.{'recompute' if in_bwd else 'fwd'}")
             if torch.is_grad_enabled() and not in_bwd and args and isinstance(args[0], torch.Tensor) \
                     and args[0].requires_grad:
                 args[0].register_hook(lambda g, bi=bi: self._post_backward(bi))
@@ -296,10 +298,12 @@ class FullyShardedModel(nn.Module):
             if torch.is_grad_enabled() and not _in_backward() and isinstance(out, torch.Tensor) \
                     and out.requires_grad:
                 out.register_hook(lambda g, bi=bi: self._pre_backward(bi))
+            nvtx.pop()
             return out
         return hook
 
     def _pre_backward(self, bi: int) -> None:
+        nvtx.push(f"block{bi}.bwd")
         if not self._bwd_started:
             self._bwd_started = True
             torch.autograd.Variable._execution_engine.queue_callback(self._finish_backward)
@@ -308,6 +312,7 @@ class FullyShardedModel(nn.Module):
             self._prefetch(bi - 1)
 
     def _post_backward(self, bi: int) -> None:
+        nvtx.pop()
         u = self.units[bi]
         if self._sync:
             self._reduce_scatter(u)

@@ -27,6 +27,7 @@ import torch
 import torch.distributed as dist
 import torch.nn as nn
 
+from ..observability.nvtx import nvtx_range
 from ..observability.metrics import (StepMetrics, aggregate_loss, compute_mfu, compute_throughput,
                                      estimate_flops_per_token, peak_memory_bytes)
 from ..parallel.fsdp import FullyShardedModel
@@ -74,19 +75,21 @@ def train_step(model: nn.Module, micro_batches: Sequence[Batch], optimizer: torc
         ids, labels = _move_batch(batch, device)
         local_tokens += ids.numel()
         with _maybe_no_sync(model, enabled=i < accum - 1):
-            with _autocast(model, device, config):
+            with _autocast(model, device, config), nvtx_range("forward"):
                 _, loss = model(ids, labels=labels)
             assert loss is not None, "the model must return a loss when labels are given"
             scaled = loss / accum
-            scaled.backward()
+            with nvtx_range("backward"):
+                scaled.backward()
         summed = summed + scaled.detach().float()
 
     sharded = isinstance(model, FullyShardedModel)
     if sharded:
-        norm = sharded_total_norm(model)
-        state = device_clip_state(norm, config.max_grad_norm)
-        optimizer.set_clip_state(state)  # type: ignore[attr-defined]
-        optimizer.step()
+        with nvtx_range("optimizer"):
+            norm = sharded_total_norm(model)
+            state = device_clip_state(norm, config.max_grad_norm)
+            optimizer.set_clip_state(state)  # type: ignore[attr-defined]
+            optimizer.step()
         loss_t = summed.reshape(1).clone()
         if dist.is_initialized() and ctx.dims.dp_size > 1:
             dist.all_reduce(loss_t, group=ctx.dp_group)

@@ -127,3 +127,24 @@ def _bf16_engine_worker(rank, world):
 
 def test_bf16_params_fp32_master_and_grads():
     run_distributed(_bf16_engine_worker, 2)
+
+
+def _memory_bound_worker(rank, world, limit):
+    cfg = tiny_config(parallel__sharding_strategy="FULL_SHARD", parallel__limit_all_gathers=limit,
+                      model__n_layers=4)
+    ctx = build_process_context(1, backend="gloo", verbose=False)
+    eng = build_engine(cfg, ctx)
+    blocks = eng.units[:-1]
+    slots = {s.data_ptr() for s in eng._slots}
+    assert len(slots) == (2 if limit else 3)
+    # every block's gathered parameters live in one of the rotating slots
+    assert {u.gathered.data_ptr() for u in blocks} == slots
+    _, loss = eng(torch.randint(0, 256, (2, 16)), labels=torch.randint(0, 256, (2, 16)))
+    loss.backward()
+    assert torch.isfinite(loss)
+
+
+@pytest.mark.parametrize("limit", [True, False])
+def test_gathered_blocks_are_bounded(limit):
+    """At most two (limit_all_gathers) or three gathered blocks exist at any time."""
+    run_distributed(_memory_bound_worker, 2, limit)
