@@ -19,9 +19,13 @@
 // layout; the same bytes serve as MN-major operands (a [rows][64] swizzled
 // tile is both), so nothing is transposed.  lse and D = rowsum(dO * O) rows
 // arrive by bulk copies next to the tiles, three tiles deep; S / dP are issued
-// two tiles ahead of the products that consume P / dS.  Warp 0 loads, warp 1 owns TMEM
-// and issues MMAs, warps 2-9 (two warpgroups, each taking half of a tile's
-// columns) do the elementwise part.  Bounded waits only.
+// two tiles ahead of the products that consume P / dS, and P / dS sit in two
+// shared-memory buffers, so the elementwise warps of tile i only wait for the
+// products of tile i-2.  The elementwise part reads its TMEM rows with one
+// wait, and computes P with one FFMA and one ex2 per element; the causal mask
+// is applied on the tiles that cross the diagonal only.  Warp 0 loads, warp 1
+// owns TMEM and issues MMAs, warps 2-9 (two warpgroups, each taking half of a
+// tile's columns) do the elementwise part.  Bounded waits only.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>
@@ -87,11 +91,11 @@ struct SmKV {
   static constexpr int NS = 3;                   // Q / dO / lse / D load stages
   static constexpr int Q_OFF = V_OFF + KV_TILE;
   static constexpr int O_OFF = Q_OFF + NS * QT;  // dO
-  static constexpr int P_OFF = O_OFF + NS * QT;  // P^T [128][64] bf16
-  static constexpr int DS_OFF = P_OFF + 16384;   // dS^T
-  static constexpr int LD_OFF = DS_OFF + 16384;  // NS x (lse[64], D[64]) floats
+  static constexpr int P_OFF = O_OFF + NS * QT;      // P^T [128][64] bf16, 2 buffers
+  static constexpr int DS_OFF = P_OFF + 2 * 16384;   // dS^T, 2 buffers
+  static constexpr int LD_OFF = DS_OFF + 2 * 16384;  // NS x (lse[64], D[64]) floats
   static constexpr int BAR_OFF = LD_OFF + NS * 512;
-  static constexpr int N_BARS = 14;
+  static constexpr int N_BARS = 16;
   static constexpr int TOTAL = BAR_OFF + N_BARS * 8 + 16 + 1024;
 };
 
@@ -110,8 +114,8 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* q_empty = bars + 4;  // [NS]
   uint64_t* s_full = bars + 7;   // [2]  S^T and dP^T ready
   uint64_t* s_empty = bars + 9;  // [2]
-  uint64_t* p_full = bars + 11;  // P^T / dS^T written
-  uint64_t* p_done = bars + 12;  // dV / dK MMAs of that tile finished
+  uint64_t* p_full = bars + 11;  // [2] P^T / dS^T of tile it written into buffer it & 1
+  uint64_t* p_done = bars + 13;  // [2] dV / dK MMAs of tile it (read buffer it & 1) finished
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + L::N_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -135,9 +139,9 @@ __global__ void __launch_bounds__(320, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 256);
+      mbar_init(&p_full[i], 256);
+      mbar_init(&p_done[i], 1);
     }
-    mbar_init(p_full, 256);
-    mbar_init(p_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -207,22 +211,24 @@ __global__ void __launch_bounds__(320, 1)
       if (ok && total > 0) ok = issue_s(0);
       if (ok && total > 1) ok = issue_s(1);
       for (int it = 0; it < total && ok && !*abort_flag; ++it) {
-        if (!mbar_wait(p_full, it & 1, a.err)) {
+        const int pb = it & 1;
+        if (!mbar_wait(&p_full[pb], (it >> 1) & 1, a.err)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const int st = it % NS;
         const uint32_t q0 = smem_u32(sm + L::Q_OFF + st * L::QT), o0 = smem_u32(sm + L::O_OFF + st * L::QT);
+        const uint32_t ptb = pt + pb * 16384, dsb = dst + pb * 16384;
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {
           const uint32_t pa = kk * 32;        // [128][64] K-major A tile
           const uint32_t gb = kk * 2048;      // 16 query rows of the MN-major B tile
-          umma_bf16(t_dv, sdesc_sw128(pt + pa, 16, 1024), sdesc_sw128(o0 + gb, 8192, 1024), ID_G, (it | kk) != 0);
-          umma_bf16(t_dk, sdesc_sw128(dst + pa, 16, 1024), sdesc_sw128(q0 + gb, 8192, 1024), ID_G, (it | kk) != 0);
+          umma_bf16(t_dv, sdesc_sw128(ptb + pa, 16, 1024), sdesc_sw128(o0 + gb, 8192, 1024), ID_G, (it | kk) != 0);
+          umma_bf16(t_dk, sdesc_sw128(dsb + pa, 16, 1024), sdesc_sw128(q0 + gb, 8192, 1024), ID_G, (it | kk) != 0);
         }
         umma_commit(&q_empty[st]);
-        umma_commit(p_done);
+        umma_commit(&p_done[pb]);
         if (it + 2 < total && !issue_s(it + 2)) {
           ok = false;
           break;
@@ -246,9 +252,12 @@ __global__ void __launch_bounds__(320, 1)
         break;
       }
       tc_fence_after();
-      float s[32], dp[32];
-      tmem_ld32(t_s[tb] + lo + c0, s);
-      tmem_ld32(t_dp[tb] + lo + c0, dp);
+      uint32_t sr[32], dr[32];
+      tmem_ld32_async(t_s[tb] + lo + c0, sr);
+      tmem_ld32_async(t_dp[tb] + lo + c0, dr);
+      tmem_wait_ld();
+      tmem_regs(sr);
+      tmem_regs(dr);
       tc_fence_before();
       mbar_arrive(&s_empty[tb]);
       // lse / D rows of this tile arrived with the tile's bulk copies (already
@@ -261,6 +270,8 @@ __global__ void __launch_bounds__(320, 1)
       const float* Ls = reinterpret_cast<const float*>(sm + L::LD_OFF + st * 512);
       const float* Ds = Ls + 64;
       const int q0 = (q_first + it % nqt) * BQ;
+      // only the two query tiles that overlap the diagonal of this key block are masked
+      const bool diag = (it % nqt) < BKV / BQ;
       uint32_t pp[16], pd[16];
 #pragma unroll
       for (int c = 0; c < 32; c += 2) {
@@ -268,26 +279,27 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int qc = c0 + c + e;
-          float v = exp2f(s[c + e] * a.scale_log2 - Ls[qc] * LOG2E);
-          if (q0 + qc < kr) v = 0.f;
+          float v = ex2_approx(fmaf(__uint_as_float(sr[c + e]), a.scale_log2, Ls[qc] * -LOG2E));
+          if (diag && q0 + qc < kr) v = 0.f;
           p[e] = v;
-          d[e] = v * (dp[c + e] - Ds[qc]);
+          d[e] = v * (__uint_as_float(dr[c + e]) - Ds[qc]);
         }
         pp[c / 2] = pack_bf16x2(p[0], p[1]);
         pd[c / 2] = pack_bf16x2(d[0], d[1]);
       }
-      if (it > 0) {  // the previous tile's dV/dK MMAs read the P^T / dS^T buffers
-        if (!mbar_wait(p_done, (it - 1) & 1, a.err)) {
+      // buffer it & 1 was last read by the dV / dK MMAs of tile it - 2
+      if (it > 1) {
+        if (!mbar_wait(&p_done[it & 1], ((it - 2) >> 1) & 1, a.err)) {
           ok = false;
           break;
         }
       }
-      store_row32(sm + L::P_OFF, r, half, pp);
-      store_row32(sm + L::DS_OFF, r, half, pd);
+      store_row32(sm + L::P_OFF + (it & 1) * 16384, r, half, pp);
+      store_row32(sm + L::DS_OFF + (it & 1) * 16384, r, half, pd);
       fence_proxy_async_smem();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[it & 1]);
     }
-    if (ok && total > 0 && mbar_wait(p_done, (total - 1) & 1, a.err)) {
+    if (ok && total > 0 && mbar_wait(&p_done[(total - 1) & 1], ((total - 1) >> 1) & 1, a.err)) {
       tc_fence_after();
       const long ld = (long)(a.nq + 2 * a.nkv) * HD;
       __nv_bfloat16* gk = a.dqkv + ((long)row0 + kr) * ld + (a.nq + hk) * HD;
@@ -332,9 +344,9 @@ struct SmQ {
   static constexpr int NS = 3;                   // K / V load stages
   static constexpr int K_OFF = O_OFF + QT;
   static constexpr int V_OFF = K_OFF + NS * KT;
-  static constexpr int DS_OFF = V_OFF + NS * KT;  // dS [128][64]
-  static constexpr int BAR_OFF = DS_OFF + 16384;
-  static constexpr int N_BARS = 14;
+  static constexpr int DS_OFF = V_OFF + NS * KT;  // dS [128][64], 2 buffers
+  static constexpr int BAR_OFF = DS_OFF + 2 * 16384;
+  static constexpr int N_BARS = 16;
   static constexpr int TOTAL = BAR_OFF + N_BARS * 8 + 16 + 1024;
 };
 
@@ -353,8 +365,8 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* kv_empty = bars + 4;  // [NS]
   uint64_t* s_full = bars + 7;    // [2]
   uint64_t* s_empty = bars + 9;   // [2]
-  uint64_t* p_full = bars + 11;
-  uint64_t* p_done = bars + 12;
+  uint64_t* p_full = bars + 11;   // [2] dS of key tile j written into buffer j & 1
+  uint64_t* p_done = bars + 13;   // [2] dQ MMAs of key tile j (read buffer j & 1) finished
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + L::N_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -376,9 +388,9 @@ __global__ void __launch_bounds__(320, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 256);
+      mbar_init(&p_full[i], 256);
+      mbar_init(&p_done[i], 1);
     }
-    mbar_init(p_full, 256);
-    mbar_init(p_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -442,19 +454,21 @@ __global__ void __launch_bounds__(320, 1)
       if (ok) ok = issue_s(0);
       if (ok && nkt > 1) ok = issue_s(1);
       for (int j = 0; j < nkt && ok && !*abort_flag; ++j) {
-        if (!mbar_wait(p_full, j & 1, a.err)) {
+        const int pb = j & 1;
+        if (!mbar_wait(&p_full[pb], (j >> 1) & 1, a.err)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const int st = j % NS;
         const uint32_t k0 = smem_u32(sm + L::K_OFF + st * L::KT);
+        const uint32_t dsb = dsa + pb * 16384;
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk)
-          umma_bf16(t_dq, sdesc_sw128(dsa + kk * 32, 16, 1024), sdesc_sw128(k0 + kk * 2048, 8192, 1024), ID_Q,
+          umma_bf16(t_dq, sdesc_sw128(dsb + kk * 32, 16, 1024), sdesc_sw128(k0 + kk * 2048, 8192, 1024), ID_Q,
                     (j | kk) != 0);
         umma_commit(&kv_empty[st]);
-        umma_commit(p_done);
+        umma_commit(&p_done[pb]);
         if (j + 2 < nkt && !issue_s(j + 2)) {
           ok = false;
           break;
@@ -479,11 +493,16 @@ __global__ void __launch_bounds__(320, 1)
         break;
       }
       tc_fence_after();
-      float s[32], dp[32];
-      tmem_ld32(t_s[tb] + lo + c0, s);
-      tmem_ld32(t_dp[tb] + lo + c0, dp);
+      uint32_t sr[32], dr[32];
+      tmem_ld32_async(t_s[tb] + lo + c0, sr);
+      tmem_ld32_async(t_dp[tb] + lo + c0, dr);
+      tmem_wait_ld();
+      tmem_regs(sr);
+      tmem_regs(dr);
       tc_fence_before();
       mbar_arrive(&s_empty[tb]);
+      // key tiles that reach past the first query row of this tile hold masked columns
+      const bool diag = j * BKV + BKV - 1 > q0;
       uint32_t pd[16];
 #pragma unroll
       for (int c = 0; c < 32; c += 2) {
@@ -491,23 +510,24 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int kc = j * BKV + c0 + c + e;
-          float p = exp2f(s[c + e] * a.scale_log2 - L2);
-          if (kc > qr) p = 0.f;
-          d[e] = p * (dp[c + e] - Dr);
+          float p = ex2_approx(fmaf(__uint_as_float(sr[c + e]), a.scale_log2, -L2));
+          if (diag && kc > qr) p = 0.f;
+          d[e] = p * (__uint_as_float(dr[c + e]) - Dr);
         }
         pd[c / 2] = pack_bf16x2(d[0], d[1]);
       }
-      if (j > 0) {
-        if (!mbar_wait(p_done, (j - 1) & 1, a.err)) {
+      // buffer j & 1 was last read by the dQ MMAs of key tile j - 2
+      if (j > 1) {
+        if (!mbar_wait(&p_done[j & 1], ((j - 2) >> 1) & 1, a.err)) {
           ok = false;
           break;
         }
       }
-      store_row32(sm + L::DS_OFF, r, half, pd);
+      store_row32(sm + L::DS_OFF + (j & 1) * 16384, r, half, pd);
       fence_proxy_async_smem();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[j & 1]);
     }
-    if (ok && mbar_wait(p_done, (nkt - 1) & 1, a.err)) {
+    if (ok && mbar_wait(&p_done[(nkt - 1) & 1], ((nkt - 1) >> 1) & 1, a.err)) {
       tc_fence_after();
       const long ld = (long)(a.nq + 2 * a.nkv) * HD;
       __nv_bfloat16* gq = a.dqkv + ((long)row0 + qr) * ld + h * HD;

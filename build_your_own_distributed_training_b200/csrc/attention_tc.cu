@@ -3,22 +3,26 @@
 //
 // One CTA per (128-row query tile, head, batch); 6 warps:
 //   warp 0     TMA producer: the Q tile once, then K and V tiles (128 keys)
-//              into a 2-deep ring, straight from the packed qkv projection;
+//              into 2-deep rings, straight from the packed qkv projection;
 //   warp 1     owns TMEM (512 columns: two 128-column S buffers + the O
 //              accumulator) and one thread issues the MMAs:
 //                S_j = Q K_j^T   (M=128, N=128, K=hd; both operands K-major)
 //                O  += P_j V_j   (M=128, N=hd,  K=128; V is MN-major)
 //              S_{j+1} is computed while the softmax warps work on S_j;
 //   warps 2-5  softmax: thread t owns query row t (TMEM lane t), reads its S
-//              row with tcgen05.ld, applies the causal mask and the online
-//              softmax in exp2 form, writes P_j in bf16 to shared memory in the
-//              128-byte-swizzled K-major layout the MMA reads, and finally
-//              normalises O and writes it out with the log-sum-exp.
+//              row with four tcgen05.ld and one wait, applies the causal mask
+//              (diagonal tile only) and the online softmax in exp2 form with
+//              the scale folded into one FFMA, writes P_j in bf16 to one of
+//              two shared-memory buffers in the 128-byte-swizzled K-major
+//              layout the MMA reads, and finally normalises O and writes it
+//              out with the log-sum-exp.  With two P buffers the softmax of
+//              tile j only waits for the PV product of tile j-2 (normally long
+//              done), so it runs concurrently with PV_{j-1} and S_{j+1}.
 //
 // O is rescaled only when a row's running maximum grows by more than 8 (in
 // log2 units): until then P = exp2(s - m_stale) <= 2^8, which fp32 and bf16
 // hold exactly as well, and the final 1/l uses the same stale maximum, so
-// the result is the same softmax.
+// the result is the same softmax.  A rescale waits for PV_{j-1} first.
 //
 // Every mbarrier wait is bounded (common.cuh); no TMA multicast.
 #include <ATen/cuda/CUDAContext.h>
@@ -63,9 +67,9 @@ struct Smem {
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + Q_BYTES;         // 2 stages
   static constexpr int V_OFF = K_OFF + 2 * K_BYTES;     // 2 stages
-  static constexpr int P_OFF = V_OFF + 2 * V_BYTES;
-  static constexpr int BAR_OFF = P_OFF + P_BYTES;
-  static constexpr int N_BARS = 16;
+  static constexpr int P_OFF = V_OFF + 2 * V_BYTES;   // 2 buffers
+  static constexpr int BAR_OFF = P_OFF + 2 * P_BYTES;
+  static constexpr int N_BARS = 18;
   static constexpr int TOTAL = BAR_OFF + N_BARS * 8 + 16 + 1024;
 };
 
@@ -90,10 +94,10 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* k_empty = bars + 3;    // [2]
   uint64_t* s_full = bars + 5;     // [2]
   uint64_t* s_empty = bars + 7;    // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* o_done = bars + 10;
-  uint64_t* v_full = bars + 11;    // [2]
-  uint64_t* v_empty = bars + 13;   // [2]
+  uint64_t* p_full = bars + 9;     // [2]: P_j written into buffer j & 1
+  uint64_t* o_done = bars + 11;    // [2]: PV_j (read P buffer j & 1) finished
+  uint64_t* v_full = bars + 13;    // [2]
+  uint64_t* v_empty = bars + 15;   // [2]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + L::N_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -114,9 +118,9 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
     }
-    mbar_init(p_full, 128);
-    mbar_init(o_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_qk);
@@ -194,8 +198,9 @@ __global__ void __launch_bounds__(192, 1)
       if (ok) ok = issue_s(0);
       if (ok && nkb > 1) ok = issue_s(1);
       for (int j = 0; j < nkb && ok && !*abort_flag; ++j) {
-        // P_j written (and O rescaled) by the softmax warps
-        if (!mbar_wait(p_full, j & 1, a.err)) {
+        // P_j written (and O rescaled if needed) by the softmax warps
+        const int pb = j & 1;
+        if (!mbar_wait(&p_full[pb], (j >> 1) & 1, a.err)) {
           ok = false;
           break;
         }
@@ -206,14 +211,15 @@ __global__ void __launch_bounds__(192, 1)
         }
         tc_fence_after();
         const uint32_t v0 = smem_u32(sm + L::V_OFF + st * L::V_BYTES);
+        const uint32_t pj = p0 + pb * L::P_BYTES;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint32_t pa = p0 + (kk >> 2) * 16384 + (kk & 3) * 32;
+          const uint32_t pa = pj + (kk >> 2) * 16384 + (kk & 3) * 32;
           const uint32_t vb = v0 + (kk >> 2) * (HD / 64) * 8192 + (kk & 3) * 2048;
           umma_bf16(t_o, sdesc_sw128(pa, 16, 1024), sdesc_sw128(vb, 8192, 1024), ID_O, (j | kk) != 0);
         }
         umma_commit(&v_empty[st]);
-        umma_commit(o_done);
+        umma_commit(&o_done[pb]);
         if (j + 2 < nkb && !issue_s(j + 2)) {
           ok = false;
           break;
@@ -226,8 +232,7 @@ __global__ void __launch_bounds__(192, 1)
     const int quad = warp & 3;
     const int r = quad * 32 + lane;          // row within the tile == TMEM lane
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    uint8_t* P = sm + L::P_OFF;
-    float m_used = -INFINITY, l = 0.f;
+    float m_used = -INFINITY, l = 0.f;       // running max (log2 units) and sum
     bool ok = true;
     for (int j = 0; j < nkb; ++j) {
       const int st = j & 1;
@@ -236,20 +241,31 @@ __global__ void __launch_bounds__(192, 1)
         break;
       }
       tc_fence_after();
-      float s[BN];
+      uint32_t sr[4][32];
 #pragma unroll
-      for (int c = 0; c < BN; c += 32) tmem_ld32(t_s[st] + lane_off + c, *reinterpret_cast<float(*)[32]>(&s[c]));
+      for (int c = 0; c < 4; ++c) tmem_ld32_async(t_s[st] + lane_off + c * 32, sr[c]);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_regs(sr[c]);
       tc_fence_before();
       mbar_arrive(&s_empty[st]);  // S buffer free for S_{j+2}
-      const bool diag = (j == qb);
-      float mx = -INFINITY;
+      float s[BN];
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        float v = s[c] * a.scale_log2;
-        if (diag && c > r) v = -INFINITY;
-        s[c] = v;
-        mx = fmaxf(mx, v);
+      for (int c = 0; c < BN; ++c) s[c] = __uint_as_float(sr[c >> 5][c & 31]);
+      if (j == qb) {
+        // diagonal tile: key column c is visible to query row r iff c <= r
+#pragma unroll
+        for (int c = 0; c < BN; ++c)
+          if (c > r) s[c] = -INFINITY;
       }
+      // row max of the raw scores, four independent chains
+      float mx4[4] = {s[0], s[1], s[2], s[3]};
+#pragma unroll
+      for (int c = 4; c < BN; c += 4) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) mx4[i] = fmaxf(mx4[i], s[c + i]);
+      }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
       float alpha = 1.f;
       bool rescale = false;
       if (mx > m_used + RESCALE_THRESHOLD) {
@@ -257,24 +273,27 @@ __global__ void __launch_bounds__(192, 1)
         rescale = (m_used != -INFINITY);
         m_used = mx;
       }
-      float rs = 0.f;
+      // p = 2^(s * scale*log2e - m): one FFMA and one ex2 per element
+      const float neg_m = -m_used;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t pk[BN / 2];
 #pragma unroll
       for (int c = 0; c < BN; c += 2) {
-        const float p0 = exp2f(s[c] - m_used), p1 = exp2f(s[c + 1] - m_used);
-        rs += p0 + p1;
+        const float p0 = ex2_approx(fmaf(s[c], a.scale_log2, neg_m));
+        const float p1 = ex2_approx(fmaf(s[c + 1], a.scale_log2, neg_m));
+        rs4[(c >> 1) & 3] += p0 + p1;
         pk[c / 2] = pack_bf16x2(p0, p1);
       }
-      l = l * alpha + rs;
-      // PV_{j-1} must be finished: it reads the P buffer and accumulates O
-      if (j > 0) {
-        if (!mbar_wait(o_done, (j - 1) & 1, a.err)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-      }
+      l = l * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
       if (__any_sync(0xffffffffu, rescale)) {
+        // O holds PV_0..PV_{j-1}: wait for the last of them, then scale it
+        if (j > 0) {
+          if (!mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, a.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
         const float f = rescale ? alpha : 1.f;
 #pragma unroll 1
         for (int c = 0; c < HD; c += 32) {
@@ -286,7 +305,15 @@ __global__ void __launch_bounds__(192, 1)
         }
         tmem_st_wait();
       }
+      // P buffer j & 1 was last read by PV_{j-2}
+      if (j > 1) {
+        if (!mbar_wait(&o_done[j & 1], ((j - 2) >> 1) & 1, a.err)) {
+          ok = false;
+          break;
+        }
+      }
       // P row r -> two 64-column atoms, 16-byte chunks XOR-swizzled by (r % 8)
+      uint8_t* P = sm + L::P_OFF + (j & 1) * L::P_BYTES;
 #pragma unroll
       for (int ch = 0; ch < BN / 8; ++ch) {
         const int atom = ch >> 3, cc = ch & 7;
@@ -299,9 +326,9 @@ __global__ void __launch_bounds__(192, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[j & 1]);
     }
-    if (ok && mbar_wait(o_done, (nkb - 1) & 1, a.err)) {
+    if (ok && mbar_wait(&o_done[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1, a.err)) {
       tc_fence_after();
       const float inv = 1.f / l;
       const long orow = (long)row0 + qb * BM + r;

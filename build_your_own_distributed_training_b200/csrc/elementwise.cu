@@ -141,13 +141,25 @@ __global__ void __launch_bounds__(NT) rmsnorm_bwd_kernel(const __nv_bfloat16* __
   for (int c = threadIdx.x; c < D; c += NT) part[(long)blockIdx.x * D + c] = dw_s[c];
 }
 
-// acc[c] += sum_b part[b, c]   (fixed order over b)
-__global__ void reduce_partials_kernel(const float* __restrict__ part, float* __restrict__ acc, int nparts, int D) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= D) return;
+// acc[c] += sum_b part[b, c] in a fixed order: block = 8 warps x 32 columns;
+// warp w sums parts w, w+8, w+16, ... (one coalesced 128-byte row segment per
+// load), then the 8 warp sums are added in warp order.
+__global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __restrict__ part, float* __restrict__ acc,
+                                                              int nparts, int D) {
+  __shared__ float red[8][32];
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const int c = blockIdx.x * 32 + l;
   float s = 0.f;
-  for (int b = 0; b < nparts; ++b) s += part[(long)b * D + c];
-  acc[c] += s;
+  if (c < D)
+    for (int b = w; b < nparts; b += 8) s += part[(long)b * D + c];
+  red[w][l] = s;
+  __syncthreads();
+  if (w == 0 && c < D) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += red[i][l];
+    acc[c] += t;
+  }
 }
 
 // ---------------------------------------------------------------- RoPE
@@ -336,12 +348,34 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
 }
 
 // ---------------------------------------------------------------- sum of squares
+// per-block partial sums of x^2: 16-byte loads, four independent accumulators
+// per thread (64 bytes in flight), fixed grid and order -> deterministic
 template <int NT>
 __global__ void __launch_bounds__(NT) sumsq_part_kernel(const float* __restrict__ x, long n, float* __restrict__ part) {
   __shared__ float red[32];
-  float s = 0.f;
-  for (long i = blockIdx.x * (long)NT + threadIdx.x; i < n; i += (long)gridDim.x * NT) s += x[i] * x[i];
-  s = block_sum<NT>(s, red);
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  // scalar head up to the first 16-byte boundary, float4 body, scalar tail
+  const long head = min(n, (long)(((16 - (reinterpret_cast<uintptr_t>(x) & 15)) & 15) / 4));
+  const long nv = (n - head) / 4;
+  const float4* xv = reinterpret_cast<const float4*>(x + head);
+  const long stride = (long)gridDim.x * NT;
+  long i = blockIdx.x * (long)NT + threadIdx.x;
+  for (; i + 3 * stride < nv; i += 4 * stride) {
+    const float4 a = xv[i], b = xv[i + stride], c = xv[i + 2 * stride], d = xv[i + 3 * stride];
+    s0 += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+    s1 += b.x * b.x + b.y * b.y + b.z * b.z + b.w * b.w;
+    s2 += c.x * c.x + c.y * c.y + c.z * c.z + c.w * c.w;
+    s3 += d.x * d.x + d.y * d.y + d.z * d.z + d.w * d.w;
+  }
+  for (; i < nv; i += stride) {
+    const float4 a = xv[i];
+    s0 += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+  }
+  if (blockIdx.x == 0) {
+    for (long t = threadIdx.x; t < head; t += NT) s1 += x[t] * x[t];
+    for (long t = head + nv * 4 + threadIdx.x; t < n; t += NT) s1 += x[t] * x[t];
+  }
+  float s = block_sum<NT>((s0 + s1) + (s2 + s3), red);
   if (threadIdx.x == 0) part[blockIdx.x] = s;
 }
 
@@ -397,7 +431,7 @@ void rmsnorm_bwd_launch(const __nv_bfloat16* dy, const __nv_bfloat16* x, const v
   else
     rmsnorm_bwd_kernel<__nv_bfloat16, 256><<<nb, 256, sh, st>>>(dy, x, (const __nv_bfloat16*)w, rstd, dx, part, M, D,
                                                                  rows_per_cta);
-  reduce_partials_kernel<<<(D + 255) / 256, 256, 0, st>>>(part, dw_acc, nb, D);
+  reduce_partials_kernel<<<(D + 31) / 32, 256, 0, st>>>(part, dw_acc, nb, D);
 }
 
 int rmsnorm_bwd_rows_per_cta(int M) {
@@ -536,7 +570,7 @@ torch::Tensor sumsq(torch::Tensor x) {
   TORCH_CHECK(x.scalar_type() == at::kFloat && x.is_contiguous(), "sumsq: contiguous fp32");
   const c10::cuda::CUDAGuard g(x.device());
   const long n = x.numel();
-  const int nb = 148 * 4;
+  const int nb = 148 * 8;
   auto part = torch::empty({nb}, x.options());
   auto out = torch::empty({}, x.options());
   auto st = cur_stream();

@@ -63,6 +63,7 @@ struct GemmArgs {
   long ldd2;
   int ffn;
   int m_blocks, n_blocks, k_iters, num_tiles;
+  int flag_tiles;       // EPI_PEER_AR: flag slots per rank (one per 128-row slab x column block)
   int* err;
   // EPI_PEER_AR: symmetric heaps of the group, staging area and flags inside them
   uint8_t* peer_base[MAX_PEERS];
@@ -86,10 +87,10 @@ __device__ __forceinline__ void tile_coords(int tile, int mblocks, int nblocks, 
   nb = r / gm;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool PAIR = false>
 struct SmemLayout {
   static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;  // a CTA pair splits B by columns
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
   static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 4) * 8 + 16 + 1024;  // + alignment slack
@@ -273,7 +274,7 @@ __device__ __forceinline__ void peer_ar_stage(const GemmArgs& a, uint32_t tbase,
 // the other lanes' staging stores before the releasing lane's flag store, and
 // release is cumulative, so one system-scope release per peer suffices.
 __device__ __forceinline__ void peer_ar_publish(const GemmArgs& a, int tile, int quad, int lane) {
-  const long nflags = (long)a.num_tiles * 4;
+  const long nflags = (long)a.flag_tiles * 4;
   const long f = (long)tile * 4 + quad;
   __syncwarp();
   if (lane < a.peer_n)
@@ -289,7 +290,7 @@ template <int BN>
 __device__ __forceinline__ bool peer_ar_finish(const GemmArgs& a, int tile, int mb, int nb, int quad, int lane) {
   const int row = mb * BM + quad * 32 + lane;
   const int n0 = nb * BN;
-  const long nflags = (long)a.num_tiles * 4;
+  const long nflags = (long)a.flag_tiles * 4;
   const long f = (long)tile * 4 + quad;
   const uint32_t* mine = reinterpret_cast<const uint32_t*>(a.peer_base[a.peer_rank] + a.flag_off);
   bool ok = true;
@@ -356,11 +357,23 @@ __device__ __forceinline__ bool peer_ar_finish(const GemmArgs& a, int tile, int 
 }
 
 // ---------------------------------------------------------------- kernel
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+// PAIR = false: one CTA per 128 x BN tile.
+// PAIR = true (BN = 256): a (2,1,1) cluster computes a 256 x 256 tile with
+// cta_group::2 MMAs: CTA r loads rows [128r, 128r+128) of the A tile and
+// columns [128r, 128r+128) of the B tile into its own shared memory, the
+// leader (r = 0) issues M=256 MMAs that read both CTAs' operands, and CTA r's
+// TMEM receives output rows [128r, 128r+128).  Each SM then streams half of
+// B per tile, which halves its shared-memory operand traffic.  Both CTAs'
+// loads count on the leader's "full" barrier; the leader's commits arrive on
+// both CTAs' "empty" / "accumulator full" barriers; both CTAs' epilogue warps
+// arrive on the leader's "accumulator empty" barrier.
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(320, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const GemmArgs args) {
-  using L = SmemLayout<BN, STAGES>;
+  static_assert(!PAIR || BN == 256, "CTA pairs use 256-column tiles");
+  using L = SmemLayout<BN, STAGES, PAIR>;
+  constexpr int TILE_M = PAIR ? 2 * BM : BM;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
@@ -372,6 +385,10 @@ __global__ void __launch_bounds__(320, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t cta = PAIR ? cluster_ctarank() : 0;   // rank within the pair
+  const bool leader = cta == 0;
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;      // tile-walker id
+  const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -380,22 +397,29 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 128);
+      mbar_init(&acc_empty[i], PAIR ? 8 : 4);  // one arrival per epilogue warp of each CTA
     }
     *abort_flag = 0;
-    fence_mbar_init();
+    if constexpr (PAIR) fence_mbar_init_cluster();
+    else fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, 2 * BN);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_holder, 2 * BN);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_holder, 2 * BN);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the peer's barriers exist before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-  constexpr uint32_t IDESC = idesc_bf16(BM, BN, A_MN, B_MN);
+  constexpr uint32_t IDESC = idesc_bf16(TILE_M, BN, A_MN, B_MN);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -405,9 +429,10 @@ __global__ void __launch_bounds__(320, 1)
       bool issued[STAGES];
       for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_phase[s] = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x) {
+      for (int tile = unit; tile < args.num_tiles && ok; tile += units) {
         int mb, nb;
         tile_coords(tile, args.m_blocks, args.n_blocks, mb, nb);
+        const int arow = mb * TILE_M + (int)cta * BM;  // first A row this CTA loads
         for (int k = 0; k < args.k_iters; ++k) {
           if (*abort_flag || !mbar_wait(&empty[stage], phase ^ 1, args.err)) {
             *abort_flag = 1;
@@ -416,41 +441,62 @@ __global__ void __launch_bounds__(320, 1)
           }
           uint8_t* sa = smem + stage * L::STAGE_BYTES;
           uint8_t* sb = sa + L::A_BYTES;
-          mbar_arrive_expect_tx(&full[stage], L::STAGE_BYTES);
-          if (!A_MN) {
-            tma_load_2d(sa, &tmA, &full[stage], k * BK, mb * BM);
-          } else {
-            tma_load_2d(sa, &tmA, &full[stage], mb * BM, k * BK);
-            tma_load_2d(sa + 8192, &tmA, &full[stage], mb * BM + 64, k * BK);
-          }
-          if (!B_MN) {
+          if constexpr (PAIR) {
+            // both CTAs' bytes complete on the leader's barrier; only the leader expects them
+            if (leader) mbar_arrive_expect_tx(&full[stage], 2 * L::STAGE_BYTES);
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+            if (!A_MN) {
+              tma_load_2d_pair(sa, &tmA, fb, k * BK, arow);
+            } else {
+              tma_load_2d_pair(sa, &tmA, fb, arow, k * BK);
+              tma_load_2d_pair(sa + 8192, &tmA, fb, arow + 64, k * BK);
+            }
+            if (!B_MN) {
+              const int r = (EPI == EPI_SWIGLU) ? (cta == 0 ? nb * 128 : args.ffn + nb * 128) : nb * BN + (int)cta * 128;
+              tma_load_2d_pair(sb, &tmB, fb, k * BK, r);
+            } else {
 #pragma unroll
-            for (int j = 0; j < BN / 128; ++j) {
-              int r = (EPI == EPI_SWIGLU) ? (j == 0 ? nb * 128 : args.ffn + nb * 128) : nb * BN + j * 128;
-              tma_load_2d(sb + j * 16384, &tmB, &full[stage], k * BK, r);
+              for (int j = 0; j < 2; ++j) tma_load_2d_pair(sb + j * 8192, &tmB, fb, nb * BN + (int)cta * 128 + j * 64, k * BK);
             }
           } else {
+            mbar_arrive_expect_tx(&full[stage], L::STAGE_BYTES);
+            if (!A_MN) {
+              tma_load_2d(sa, &tmA, &full[stage], k * BK, arow);
+            } else {
+              tma_load_2d(sa, &tmA, &full[stage], arow, k * BK);
+              tma_load_2d(sa + 8192, &tmA, &full[stage], arow + 64, k * BK);
+            }
+            if (!B_MN) {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 8192, &tmB, &full[stage], nb * BN + j * 64, k * BK);
+              for (int j = 0; j < BN / 128; ++j) {
+                int r = (EPI == EPI_SWIGLU) ? (j == 0 ? nb * 128 : args.ffn + nb * 128) : nb * BN + j * 128;
+                tma_load_2d(sb + j * 16384, &tmB, &full[stage], k * BK, r);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 8192, &tmB, &full[stage], nb * BN + j * 64, k * BK);
+            }
           }
           issued[stage] = true;
           issued_phase[stage] = phase;
           if (++stage == STAGES) stage = 0, phase ^= 1;
         }
       }
-      if (!ok) {
+      if (!ok && leader) {
         // drain copies still in flight before the CTA's shared memory goes away
+        // (a pair's follower has no barrier of its own for them: its bounded
+        // waits outlast its last copy by far)
         for (int s = 0; s < STAGES; ++s)
           if (issued[s]) mbar_wait(&full[s], issued_phase[s], args.err);
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       int stage = 0;
       uint32_t phase = 0;
       int t = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x, ++t) {
+      for (int tile = unit; tile < args.num_tiles && ok; tile += units, ++t) {
         const int acc = t & 1;
         const uint32_t acc_phase = (t >> 1) & 1;
         if (*abort_flag || !mbar_wait(&acc_empty[acc], acc_phase ^ 1, args.err)) {
@@ -472,50 +518,60 @@ __global__ void __launch_bounds__(320, 1)
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t ad = A_MN ? sdesc_sw128(a0 + kk * 2048, 8192, 1024) : sdesc_sw128(a0 + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? sdesc_sw128(b0 + kk * 2048, 8192, 1024) : sdesc_sw128(b0 + kk * 32, 16, 1024);
-            umma_bf16(d, ad, bd, IDESC, (k | kk) != 0);
+            if constexpr (PAIR) umma_bf16_pair(d, ad, bd, IDESC, (k | kk) != 0);
+            else umma_bf16(d, ad, bd, IDESC, (k | kk) != 0);
           }
-          umma_commit(&empty[stage]);
+          if constexpr (PAIR) umma_commit_pair(&empty[stage]);
+          else umma_commit(&empty[stage]);
           if (++stage == STAGES) stage = 0, phase ^= 1;
         }
-        umma_commit(&acc_full[acc]);
+        if constexpr (PAIR) umma_commit_pair(&acc_full[acc]);
+        else umma_commit(&acc_full[acc]);
       }
     }
   } else {
-    // two epilogue warpgroups (warps 2-5 and 6-9): group g drains the tiles
-    // that land in TMEM buffer g, so each group has two tiles of time for its
-    // stores and twice as many memory requests are in flight per SM
+    // two epilogue warpgroups (warps 2-9): group g drains the tiles that land
+    // in TMEM buffer g, so each group has two tiles of time for its stores
+    // and twice as many memory requests are in flight per SM
     const int quad = warp & 3;
     const int wg = (warp - 2) >> 2;
     int t = 0;
     int pend_tile = -1, pend_mb = 0, pend_nb = 0;  // EPI_PEER_AR: tile published, not yet reduced
-    for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++t) {
+    for (int tile = unit; tile < args.num_tiles; tile += units, ++t) {
       const int acc = t & 1;
       if (acc != wg) continue;
       const uint32_t acc_phase = (t >> 1) & 1;
       int mb, nb;
       tile_coords(tile, args.m_blocks, args.n_blocks, mb, nb);
+      const int slab = PAIR ? 2 * mb + (int)cta : mb;     // this CTA's 128-row block of the output
+      const int ftile = PAIR ? 2 * tile + (int)cta : tile;
       if (*abort_flag || !mbar_wait(&acc_full[acc], acc_phase, args.err)) {
         *abort_flag = 1;
         break;
       }
       tc_fence_after();
       if constexpr (EPI == EPI_PEER_AR) {
-        peer_ar_stage<BN>(args, tmem_base + acc * BN, mb, nb, quad, lane);
-        tc_fence_before();
-        mbar_arrive(&acc_empty[acc]);  // the MMA warp may reuse this buffer while we exchange
-        peer_ar_publish(args, tile, quad, lane);
+        peer_ar_stage<BN>(args, tmem_base + acc * BN, slab, nb, quad, lane);
+      } else {
+        epilogue_tile<BN, EPI>(args, tmem_base + acc * BN, slab, nb, quad, lane);
+      }
+      // the MMA warp may reuse this accumulator buffer
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (PAIR) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));
+        else mbar_arrive(&acc_empty[acc]);
+      }
+      if constexpr (EPI == EPI_PEER_AR) {
+        peer_ar_publish(args, ftile, quad, lane);
         if (pend_tile >= 0 && !peer_ar_finish<BN>(args, pend_tile, pend_mb, pend_nb, quad, lane)) {
           *abort_flag = 1;
           pend_tile = -1;
           break;
         }
-        pend_tile = tile;
-        pend_mb = mb;
+        pend_tile = ftile;
+        pend_mb = slab;
         pend_nb = nb;
-      } else {
-        epilogue_tile<BN, EPI>(args, tmem_base + acc * BN, mb, nb, quad, lane);
-        tc_fence_before();
-        mbar_arrive(&acc_empty[acc]);
       }
     }
     if constexpr (EPI == EPI_PEER_AR) {
@@ -524,8 +580,12 @@ __global__ void __launch_bounds__(320, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // no remote arrive or MMA operand read targets a CTA that has left
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, 2 * BN);
+  if (warp == 1) {
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, 2 * BN);
+    else tmem_dealloc(tmem_base, 2 * BN);
+  }
 }
 
 // ---------------------------------------------------------------- host side
@@ -577,42 +637,71 @@ static int num_sms() {
   return n;
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool PAIR>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t st) {
-  using L = SmemLayout<BN, STAGES>;
-  auto kern = gemm_tcgen05_kernel<BN, STAGES, A_MN, B_MN, EPI>;
+  using L = SmemLayout<BN, STAGES, PAIR>;
+  auto kern = gemm_tcgen05_kernel<BN, STAGES, A_MN, B_MN, EPI, PAIR>;
   static bool configured = false;
   if (!configured) {
     DTB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
     configured = true;
   }
-  const int grid = std::min(g.num_tiles, num_sms());
-  if (grid == 0) return;
-  kern<<<grid, 320, L::TOTAL, st>>>(ta, tb, g);
+  if (g.num_tiles == 0) return;
+  if constexpr (PAIR) {
+    // persistent (2,1,1) clusters, one per pair of SMs
+    const int pairs = std::min(g.num_tiles, num_sms() / 2);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(320, 1, 1);
+    cfg.dynamicSmemBytes = L::TOTAL;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    DTB_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, g));
+  } else {
+    const int grid = std::min(g.num_tiles, num_sms());
+    kern<<<grid, 320, L::TOTAL, st>>>(ta, tb, g);
+  }
   DTB_LAUNCH_CHECK();
 }
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, bool PAIR>
 static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t st) {
-  constexpr int ST = BN == 256 ? 4 : 6;
+  // per-CTA stage: 16 KB of A + 32 KB (BN=256), 16 KB (BN=128 or a pair's half of 256) of B
+  constexpr int ST = (BN == 256 && !PAIR) ? 4 : 6;
   switch (epi) {
-    case EPI_STORE_BF16: launch<BN, ST, A_MN, B_MN, EPI_STORE_BF16>(ta, tb, g, st); break;
-    case EPI_STORE_F32: launch<BN, ST, A_MN, B_MN, EPI_STORE_F32>(ta, tb, g, st); break;
-    case EPI_ACC_F32: launch<BN, ST, A_MN, B_MN, EPI_ACC_F32>(ta, tb, g, st); break;
+    case EPI_STORE_BF16: launch<BN, ST, A_MN, B_MN, EPI_STORE_BF16, PAIR>(ta, tb, g, st); break;
+    case EPI_STORE_F32: launch<BN, ST, A_MN, B_MN, EPI_STORE_F32, PAIR>(ta, tb, g, st); break;
+    case EPI_ACC_F32: launch<BN, ST, A_MN, B_MN, EPI_ACC_F32, PAIR>(ta, tb, g, st); break;
     case EPI_RESIDUAL:
-      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_RESIDUAL>(ta, tb, g, st); break; }
+      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_RESIDUAL, PAIR>(ta, tb, g, st); break; }
       TORCH_CHECK(false, "residual epilogue needs K-major operands");
     case EPI_ROPE:
-      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_ROPE>(ta, tb, g, st); break; }
+      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_ROPE, PAIR>(ta, tb, g, st); break; }
       TORCH_CHECK(false, "rope epilogue needs K-major operands");
     case EPI_SWIGLU:
-      if constexpr (!A_MN && !B_MN && BN == 256) { launch<BN, ST, A_MN, B_MN, EPI_SWIGLU>(ta, tb, g, st); break; }
+      if constexpr (!A_MN && !B_MN && BN == 256) { launch<BN, ST, A_MN, B_MN, EPI_SWIGLU, PAIR>(ta, tb, g, st); break; }
       TORCH_CHECK(false, "swiglu epilogue needs K-major operands and BN=256");
     case EPI_PEER_AR:
-      if constexpr (!A_MN) { launch<BN, ST, A_MN, B_MN, EPI_PEER_AR>(ta, tb, g, st); break; }
+      if constexpr (!A_MN) { launch<BN, ST, A_MN, B_MN, EPI_PEER_AR, PAIR>(ta, tb, g, st); break; }
       TORCH_CHECK(false, "peer all-reduce epilogue needs a K-major A operand");
     default: DTB_CHECK(false, "unknown epilogue %d", epi);
   }
+}
+
+// CTA pairs for 256-column tiles unless DTB_GEMM_PAIR=0 (single-CTA tiles)
+static bool pair_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("DTB_GEMM_PAIR");
+    v = (e == nullptr || e[0] != '0') ? 1 : 0;
+  }
+  return v == 1;
 }
 
 }  // namespace dtb
@@ -709,9 +798,12 @@ static void gemm_impl(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_
     g.N = (int)NB;
     g.n_blocks = (int)((NB + BN - 1) / BN);
   }
-  g.m_blocks = (int)((M + BM - 1) / BM);
+  const bool pair = BN == 256 && M > BM && pair_enabled();
+  const int tile_m = pair ? 2 * BM : BM;
+  g.m_blocks = (int)((M + tile_m - 1) / tile_m);
   g.k_iters = (int)((K + BK - 1) / BK);
   g.num_tiles = g.m_blocks * g.n_blocks;
+  g.flag_tiles = pair ? 2 * g.num_tiles : g.num_tiles;
   TORCH_CHECK(D.size(0) == M && D.size(1) == g.N, "gemm: output shape mismatch");
   // tensor maps: A box = 128 rows (K-major) or 64 K-rows (MN-major); B likewise
   if (dtb_debug_enabled())
@@ -720,15 +812,20 @@ static void gemm_impl(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_
   const CUtensorMap ta = a_mn ? make_map(A.data_ptr(), M, K, A.stride(0), BK) : make_map(A.data_ptr(), K, M, A.stride(0), BM);
   const CUtensorMap tb = b_mn ? make_map(B.data_ptr(), NB, K, B.stride(0), BK) : make_map(B.data_ptr(), K, NB, B.stride(0), 128);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  if (BN == 256) {
-    if (!a_mn && !b_mn) dispatch_epi<256, false, false>(e, ta, tb, g, st);
-    else if (!a_mn && b_mn) dispatch_epi<256, false, true>(e, ta, tb, g, st);
-    else if (a_mn && b_mn) dispatch_epi<256, true, true>(e, ta, tb, g, st);
+  if (BN == 256 && pair) {
+    if (!a_mn && !b_mn) dispatch_epi<256, false, false, true>(e, ta, tb, g, st);
+    else if (!a_mn && b_mn) dispatch_epi<256, false, true, true>(e, ta, tb, g, st);
+    else if (a_mn && b_mn) dispatch_epi<256, true, true, true>(e, ta, tb, g, st);
+    else TORCH_CHECK(false, "gemm: layout (MN, K) not built");
+  } else if (BN == 256) {
+    if (!a_mn && !b_mn) dispatch_epi<256, false, false, false>(e, ta, tb, g, st);
+    else if (!a_mn && b_mn) dispatch_epi<256, false, true, false>(e, ta, tb, g, st);
+    else if (a_mn && b_mn) dispatch_epi<256, true, true, false>(e, ta, tb, g, st);
     else TORCH_CHECK(false, "gemm: layout (MN, K) not built");
   } else {
-    if (!a_mn && !b_mn) dispatch_epi<128, false, false>(e, ta, tb, g, st);
-    else if (!a_mn && b_mn) dispatch_epi<128, false, true>(e, ta, tb, g, st);
-    else if (a_mn && b_mn) dispatch_epi<128, true, true>(e, ta, tb, g, st);
+    if (!a_mn && !b_mn) dispatch_epi<128, false, false, false>(e, ta, tb, g, st);
+    else if (!a_mn && b_mn) dispatch_epi<128, false, true, false>(e, ta, tb, g, st);
+    else if (a_mn && b_mn) dispatch_epi<128, true, true, false>(e, ta, tb, g, st);
     else TORCH_CHECK(false, "gemm: layout (MN, K) not built");
   }
 }

@@ -18,6 +18,8 @@ import math
 import torch
 import torch.nn as nn
 
+from ..ops import grad_state
+
 
 class Linear(nn.Module):
     def __init__(self, in_features: int, out_features: int, bias: bool = False) -> None:
@@ -52,6 +54,9 @@ def fused_rows(params: list[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor |
         w = _adjacent_view(params)
         mg = _adjacent_view(grads)  # type: ignore[arg-type]
         if w is not None and mg is not None:
+            first = grad_state.tag_of(grads[0])
+            if first is not None:  # the stacked view covers the constituents' fresh ranges
+                grad_state.tag(mg, first[0], first[1])
             return w, mg
     if len(params) == 1:
         return params[0], grads[0]

@@ -12,6 +12,7 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
+from . import grad_state
 from ._ext import native
 
 
@@ -33,6 +34,7 @@ class _EmbeddingFn(torch.autograd.Function):
     def backward(ctx, dout):  # type: ignore[override]
         (tokens,) = ctx.saved_tensors
         mg = ctx.main_grad
+        grad_state.zero_if_fresh(mg)  # rows are scatter-added
         acc = mg.view(ctx.wshape) if mg is not None else torch.zeros(
             ctx.wshape, device=dout.device, dtype=torch.float32)
         if dout.is_cuda:

@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import torch
 
+from . import grad_state
 from ._ext import native
 
 # epilogue codes shared with csrc/gemm.cu
@@ -68,17 +69,26 @@ def mm_nn(a: torch.Tensor, b: torch.Tensor, *, alpha: torch.Tensor | None = None
 
 
 def mm_tn_acc(a: torch.Tensor, b: torch.Tensor, acc: torch.Tensor, *,
-              alpha: torch.Tensor | None = None) -> torch.Tensor:
-    """``acc[M,N] += a[K,M]^T @ b[K,N]`` with ``acc`` fp32 (weight gradients)."""
+              alpha: torch.Tensor | None = None, store: bool = False) -> torch.Tensor:
+    """``acc[M,N] += a[K,M]^T @ b[K,N]`` with ``acc`` fp32 (weight gradients); ``store`` overwrites."""
     if not a.is_cuda:
         y = a.t().to(acc.dtype) @ b.to(acc.dtype)
-        acc.add_(y * alpha if alpha is not None else y)
+        y = y * alpha if alpha is not None else y
+        acc.copy_(y) if store else acc.add_(y)
         return acc
     _check_cuda(a, b, acc)
     if acc.dtype != torch.float32:
         raise ValueError("mm_tn_acc accumulates into an fp32 buffer")
-    native().gemm(a, b, acc, True, True, EPI_ACC_F32, None, alpha, None, None, None, 0, 0)
+    native().gemm(a, b, acc, True, True, EPI_STORE if store else EPI_ACC_F32, None, alpha, None, None, None, 0, 0)
     return acc
+
+
+def mm_tn_into_grad(a: torch.Tensor, b: torch.Tensor, main_grad: torch.Tensor, shape, *,
+                    alpha: torch.Tensor | None = None) -> torch.Tensor:
+    """Weight gradient ``a^T b`` into a gradient slice: overwritten while the slice is
+    fresh (first writer of the step), accumulated afterwards."""
+    store = grad_state.take_fresh(main_grad)
+    return mm_tn_acc(a, b, main_grad.view(shape), alpha=alpha, store=store)
 
 
 def mm_tn(a: torch.Tensor, b: torch.Tensor, *, alpha: torch.Tensor | None = None,

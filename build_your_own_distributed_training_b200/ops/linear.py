@@ -37,7 +37,7 @@ def _input_grad(dy2: torch.Tensor, weight: torch.Tensor, grad_comm) -> torch.Ten
 def _weight_grad(dy2: torch.Tensor, x2: torch.Tensor, weight: torch.Tensor,
                  main_grad: torch.Tensor | None) -> torch.Tensor | None:
     if main_grad is not None:
-        gemm.mm_tn_acc(dy2, x2, main_grad.view(weight.shape))
+        gemm.mm_tn_into_grad(dy2, x2, main_grad, weight.shape)
         return None
     if not weight.requires_grad:
         return None

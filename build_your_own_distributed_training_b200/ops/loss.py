@@ -33,7 +33,7 @@ class _HeadCEFn(torch.autograd.Function):
         alpha = dloss.reshape(1).float().contiguous()
         dh = gemm.mm_nn(dlogits, w, alpha=alpha)
         if ctx.main_grad is not None:
-            gemm.mm_tn_acc(dlogits, h, ctx.main_grad.view(w.shape), alpha=alpha)
+            gemm.mm_tn_into_grad(dlogits, h, ctx.main_grad, w.shape, alpha=alpha)
             dw = None
         elif w.requires_grad:
             dw = gemm.mm_tn(dlogits, h, alpha=alpha).to(w.dtype)

@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import torch
 
+from . import grad_state
 from ._ext import native
 
 
@@ -39,6 +40,7 @@ class _RMSNormFn(torch.autograd.Function):
         x2, w, rstd = ctx.saved_tensors
         dy2 = dy.reshape(-1, dy.shape[-1]).contiguous()
         mg = ctx.main_grad
+        grad_state.zero_if_fresh(mg)  # the dw reduction accumulates
         if dy2.is_cuda:
             acc = mg if mg is not None else torch.zeros(w.shape, device=w.device, dtype=torch.float32)
             dx = native().rmsnorm_bwd(dy2, x2, w, rstd, acc)

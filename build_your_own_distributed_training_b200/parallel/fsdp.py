@@ -51,6 +51,7 @@ import torch.nn as nn
 
 from ..config import ParallelConfig
 from ..observability import nvtx
+from ..ops import grad_state
 from ..utils.dtype import build_mixed_precision
 from .tensor_parallel import tp_param_kind
 
@@ -88,6 +89,7 @@ class FlatUnit:
     grad_shard: torch.Tensor | None = None   # fp32 [S]
     gathered: torch.Tensor | None = None     # param_dtype [P] (persistent or slot)
     slot: int = -1
+    fresh: Any = None                        # FreshSet over ``grad`` (lazily zeroed slices)
     extras: dict = field(default_factory=dict)
 
     def shard_range(self, rank: int) -> tuple[int, int]:
@@ -246,7 +248,8 @@ class FullyShardedModel(nn.Module):
                 u.param_shard = torch.empty(u.shard_numel, dtype=pdt, device=dev)
                 u.grad = torch.empty(u.numel, dtype=torch.float32, device=dev)
             u.param_shard.copy_(u.master.to(pdt))
-            u.grad.zero_()
+            u.grad.zero_()  # padding stays zero for good; parameter slices go lazy from here
+            u.fresh = grad_state.FreshSet(u.grad)
             # unsharded units reduce in place: the gradient shard is the gradient buffer
             u.grad_shard = u.grad if self.shard_world == 1 else torch.zeros(u.shard_numel, dtype=torch.float32,
                                                                             device=dev)
@@ -273,7 +276,8 @@ class FullyShardedModel(nn.Module):
         assert u.gathered is not None and u.grad is not None
         for e in u.entries:
             e.param.data = u.gathered[e.offset:e.offset + e.numel].view(e.shape)
-            e.param.main_grad = u.grad[e.offset:e.offset + e.numel].view(e.shape)  # type: ignore[attr-defined]
+            e.param.main_grad = grad_state.tag(  # type: ignore[attr-defined]
+                u.grad[e.offset:e.offset + e.numel].view(e.shape), u.fresh, e.offset)
 
     # ------------------------------------------------------------------ hooks
     def _install_hooks(self) -> None:
@@ -377,6 +381,7 @@ class FullyShardedModel(nn.Module):
     # ------------------------------------------------------------ reduction
     def _reduce_scatter(self, u: FlatUnit) -> None:
         assert u.grad is not None and u.grad_shard is not None
+        u.fresh.flush()  # slices no kernel wrote this step are zero gradients
         if self._is_cuda:
             s = self._comm_stream
             s.wait_stream(torch.cuda.current_stream())
@@ -408,8 +413,9 @@ class FullyShardedModel(nn.Module):
             self._sync = prev
 
     def zero_grad_buffers(self) -> None:
+        """Logically zero every gradient: slices become fresh, the first writer overwrites them."""
         for u in self.units:
-            u.grad.zero_()  # type: ignore[union-attr]
+            u.fresh.mark([(e.offset, e.numel) for e in u.entries])
 
     # ------------------------------------------------------------ forward
     def forward(self, *args: Any, **kwargs: Any) -> Any:

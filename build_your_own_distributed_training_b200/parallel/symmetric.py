@@ -193,7 +193,7 @@ class _RowParallelAR(torch.autograd.Function):
         dy = dy.contiguous()
         dx = gemm.mm_nn(dy, w)  # the input is TP-sharded: no reduction needed
         if ctx.main_grad is not None:
-            gemm.mm_tn_acc(dy, x2, ctx.main_grad.view(w.shape))
+            gemm.mm_tn_into_grad(dy, x2, ctx.main_grad, w.shape)
             dw = None
         else:
             dw = gemm.mm_tn(dy, x2).to(w.dtype) if w.requires_grad else None
@@ -209,7 +209,9 @@ class TPComm:
         self.rank = dist.get_rank(group)
         self.max_tokens, self.width = max_tokens, width
         self.max_elems = max_tokens * width
-        tiles = (-(-max_tokens // 128)) * (-(-width // 128))
+        # one flag per (128-row slab, column block, quadrant, rank); +1 slab row covers
+        # 256-row CTA-pair tiles that overhang max_tokens
+        tiles = (-(-max_tokens // 128) + 1) * (-(-width // 128))
         self.flag_bytes = _align(tiles * 4 * self.size * 4)
         slot = _align(self.max_elems * 2)
         self.heap = SymmetricHeap(group, 2 * slot + self.flag_bytes + 64 * 1024, device)

@@ -96,6 +96,31 @@ def test_gemm_swiglu_epilogue():
     assert _rel(act, ref) < 2e-2
 
 
+@pytest.mark.parametrize("M,N,K", [(1024, 1024, 512), (200, 384, 256), (4096, 4096, 2048)])
+def test_gemm_peer_allreduce_emulated_partner(M, N, K):
+    """The fused GEMM + all-reduce on one GPU, the partner rank emulated by memory.
+
+    Two "ranks'" symmetric heaps are local buffers; the partner's staged
+    partial tile holds known data and its flags are set before the launch, so
+    rank 0's kernel runs its whole stage / publish / wait / pull / sum path.
+    """
+    a, b, r = _rand(M, K), _rand(N, K), _rand(M, N)
+    partner = _rand(M, N)
+    stage = M * N * 2
+    flag_off = (stage + 255) // 256 * 256
+    nflags = 2 * (M // 128 + 2) * (N // 128 + 2) * 4
+    heaps = [torch.zeros(flag_off + nflags * 4, device=DEV, dtype=torch.uint8) for _ in range(2)]
+    heaps[1][:stage].view(BF).copy_(partner.reshape(-1))
+    heaps[0][flag_off:].view(torch.int32).fill_(7)
+    out = torch.empty(M, N, device=DEV, dtype=BF)
+    native().gemm_peer_ar(a, b, out, False, r, None, [h.data_ptr() for h in heaps], 0, 0, flag_off, 7, 1.0)
+    mine = (a.float() @ b.float().t()).to(BF).float()
+    ref = mine + partner.float() + r.float()
+    assert _rel(out, ref) < 1e-2
+    # rank 0 published its own tile to the partner's flag array
+    assert int((heaps[1][flag_off:].view(torch.int32) == 7).sum()) > 0
+
+
 def test_rmsnorm_fwd_bwd():
     from build_your_own_distributed_training_b200.ops.norm import rms_norm
     x = _rand(1000, 4096).requires_grad_()
