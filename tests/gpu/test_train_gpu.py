@@ -1,0 +1,26 @@
+"""Bit-exact resume and activation-checkpointing equality on the GPU path (1 and 2 GPUs)."""
+
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("needs a GPU", allow_module_level=True)
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+@pytest.mark.parametrize("n", [1, 2])
+def test_resume_and_checkpointing_are_bit_exact(n):
+    if torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", DTB_PG_TIMEOUT_S="120")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
+           "--master-addr", "127.0.0.1", "--master-port", str(29681 + n), os.path.join(HERE, "train_worker.py")]
+    r = subprocess.run(["timeout", "-k", "30", "600"] + cmd, env=env, capture_output=True, text=True)
+    assert r.returncode == 0 and "TRAIN_OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
