@@ -282,6 +282,69 @@ __device__ __forceinline__ void peer_ar_publish(const GemmArgs& a, int tile, int
                    a.epoch);
 }
 
+// The warp owns rows [row0, row0 + 32) of a tile; lane l covers columns
+// [c, c + 8) (c = 8l), so each load instruction reads one contiguous 512-byte
+// row segment.  Per step the loads of RU rows from every rank (NP >= peer_n)
+// and of the residual are all issued before any is used (NP * RU + RU 16-byte
+// loads in flight per lane), so a step costs one NVLink round trip; the sum
+// then runs in rank order, which keeps every rank's result bitwise equal.
+template <int NP, int RU>
+__device__ __forceinline__ void peer_sum_rows(const GemmArgs& a, int row0, int n0, int c) {
+#pragma unroll 1
+  for (int r = 0; r < 32; r += RU) {
+    uint4 v[NP][RU], q[RU];
+#pragma unroll
+    for (int p = 0; p < NP; ++p)
+#pragma unroll
+      for (int i = 0; i < RU; ++i) {
+        const int rr = row0 + r + i;
+        v[p][i] = (p < a.peer_n && rr < a.M)
+                      ? ld_cg_v4(a.peer_base[p] + a.stage_off + ((long)rr * a.ldd + n0 + c) * 2)
+                      : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+    for (int i = 0; i < RU; ++i) {
+      const int rr = row0 + r + i;
+      q[i] = (a.R != nullptr && rr < a.M) ? *reinterpret_cast<const uint4*>(a.R + (long)rr * a.ldr + n0 + c)
+                                          : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int i = 0; i < RU; ++i) {
+      const int rr = row0 + r + i;
+      if (rr >= a.M) continue;
+      float acc[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        if (p >= a.peer_n) break;
+        const uint32_t* u = &v[p][i].x;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 t = unpack_bf16x2(u[k]);
+          acc[2 * k] += t.x;
+          acc[2 * k + 1] += t.y;
+        }
+      }
+      if (a.R != nullptr) {
+        const uint32_t* u = &q[i].x;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 t = unpack_bf16x2(u[k]);
+          acc[2 * k] += t.x;
+          acc[2 * k + 1] += t.y;
+        }
+      }
+      uint4 o;
+      o.x = pack_bf16x2(acc[0], acc[1]);
+      o.y = pack_bf16x2(acc[2], acc[3]);
+      o.z = pack_bf16x2(acc[4], acc[5]);
+      o.w = pack_bf16x2(acc[6], acc[7]);
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.D) + (long)rr * a.ldd + n0 + c) = o;
+    }
+  }
+}
+
 // Phase 3 (one tile later, so the flag round trip overlaps the next tile):
 // wait for every peer's copy of the tile, then sum the staged tiles in rank
 // order (+ residual) into D.  All ranks add the same bf16 partials in the same
@@ -297,62 +360,13 @@ __device__ __forceinline__ bool peer_ar_finish(const GemmArgs& a, int tile, int 
   for (int p = 0; p < a.peer_n && ok; ++p) ok = wait_flag(mine + (long)p * nflags + f, a.epoch, a.timeout_ns, a.err);
   if (!ok) return false;
   (void)row;
-  // the warp owns rows [row0, row0 + 32); lanes run across the columns so each
-  // load instruction reads one contiguous 512-byte row segment from a peer,
-  // and four rows are in flight per peer
   const int row0 = mb * BM + quad * 32;
   const int cols = min(BN, a.N - n0);
   const int c = lane * 8;
   if (c >= cols) return true;
-  constexpr int RU = 4;
-#pragma unroll 1
-  for (int r = 0; r < 32; r += RU) {
-    float acc[RU][8];
-#pragma unroll
-    for (int i = 0; i < RU; ++i)
-#pragma unroll
-      for (int k = 0; k < 8; ++k) acc[i][k] = 0.f;
-    for (int p = 0; p < a.peer_n; ++p) {
-      uint4 v[RU];
-#pragma unroll
-      for (int i = 0; i < RU; ++i) {
-        const int rr = row0 + r + i;
-        v[i] = rr < a.M ? ld_cg_v4(a.peer_base[p] + a.stage_off + ((long)rr * a.ldd + n0 + c) * 2)
-                        : make_uint4(0, 0, 0, 0);
-      }
-#pragma unroll
-      for (int i = 0; i < RU; ++i) {
-        const uint32_t* u = &v[i].x;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float2 t = unpack_bf16x2(u[k]);
-          acc[i][2 * k] += t.x;
-          acc[i][2 * k + 1] += t.y;
-        }
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < RU; ++i) {
-      const int rr = row0 + r + i;
-      if (rr >= a.M) continue;
-      if (a.R != nullptr) {
-        const uint4 q = *reinterpret_cast<const uint4*>(a.R + (long)rr * a.ldr + n0 + c);
-        const uint32_t* u = &q.x;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float2 t = unpack_bf16x2(u[k]);
-          acc[i][2 * k] += t.x;
-          acc[i][2 * k + 1] += t.y;
-        }
-      }
-      uint4 o;
-      o.x = pack_bf16x2(acc[i][0], acc[i][1]);
-      o.y = pack_bf16x2(acc[i][2], acc[i][3]);
-      o.z = pack_bf16x2(acc[i][4], acc[i][5]);
-      o.w = pack_bf16x2(acc[i][6], acc[i][7]);
-      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.D) + (long)rr * a.ldd + n0 + c) = o;
-    }
-  }
+  if (a.peer_n <= 2) peer_sum_rows<2, 8>(a, row0, n0, c);
+  else if (a.peer_n <= 4) peer_sum_rows<4, 4>(a, row0, n0, c);
+  else peer_sum_rows<8, 2>(a, row0, n0, c);
   return true;
 }
 
