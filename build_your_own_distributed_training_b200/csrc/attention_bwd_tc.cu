@@ -335,38 +335,38 @@ __global__ void __launch_bounds__(320, 1)
 }
 
 // ============================================================== dQ
-template <int HD>
+template <int HD, int STAGES = 4>
 struct SmQ {
   static constexpr int QT = 128 * HD * 2;        // Q or dO: [hd/64][128][128 B]
   static constexpr int KT = 64 * HD * 2;         // K or V tile: [hd/64][64][128 B]
   static constexpr int Q_OFF = 0;
   static constexpr int O_OFF = Q_OFF + QT;
-  static constexpr int NS = 3;                   // K / V load stages
+  static constexpr int NS = STAGES;              // K / V load stages
   static constexpr int K_OFF = O_OFF + QT;
   static constexpr int V_OFF = K_OFF + NS * KT;
   static constexpr int DS_OFF = V_OFF + NS * KT;  // dS [128][64], 2 buffers
   static constexpr int BAR_OFF = DS_OFF + 2 * 16384;
-  static constexpr int N_BARS = 16;
+  static constexpr int N_BARS = 2 * NS + 10;
   static constexpr int TOTAL = BAR_OFF + N_BARS * 8 + 16 + 1024;
 };
 
-template <int HD>
+template <int HD, int STAGES>
 __global__ void __launch_bounds__(320, 1)
     attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tm_q128, const __grid_constant__ CUtensorMap tm_do128,
                           const __grid_constant__ CUtensorMap tm_kv64, const BwdArgs a) {
-  using L = SmQ<HD>;
+  using L = SmQ<HD, STAGES>;
   constexpr int BQ = 128, BKV = 64;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR_OFF);
   constexpr int NS = L::NS;
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [NS]
-  uint64_t* kv_empty = bars + 4;  // [NS]
-  uint64_t* s_full = bars + 7;    // [2]
-  uint64_t* s_empty = bars + 9;   // [2]
-  uint64_t* p_full = bars + 11;   // [2] dS of key tile j written into buffer j & 1
-  uint64_t* p_done = bars + 13;   // [2] dQ MMAs of key tile j (read buffer j & 1) finished
+  uint64_t* kv_full = bars + 1;            // [NS]
+  uint64_t* kv_empty = bars + 1 + NS;      // [NS]
+  uint64_t* s_full = bars + 1 + 2 * NS;    // [2]
+  uint64_t* s_empty = bars + 3 + 2 * NS;   // [2]
+  uint64_t* p_full = bars + 5 + 2 * NS;    // [2] dS of key tile j written into buffer j & 1
+  uint64_t* p_done = bars + 7 + 2 * NS;    // [2] dQ MMAs of key tile j (read buffer j & 1) finished
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + L::N_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -597,16 +597,26 @@ void bwd_tc_launch(const torch::Tensor& qkv, const torch::Tensor& dO, const floa
   if (!cfg) {
     DTB_CUDA(cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   SmKV<HD>::TOTAL));
-    DTB_CUDA(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  SmQ<HD>::TOTAL));
+    DTB_CUDA(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<HD, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  SmQ<HD, 3>::TOTAL));
+    DTB_CUDA(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<HD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  SmQ<HD, 4>::TOTAL));
     cfg = true;
   }
+  // K/V ring depth of the dQ kernel: 4 unless DTB_ATTN_DQ_STAGES=3
+  static const int dq_stages = [] {
+    const char* e = getenv("DTB_ATTN_DQ_STAGES");
+    return (e != nullptr && e[0] == '3') ? 3 : 4;
+  }();
   BwdArgs args{lse, Dv, reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), S, nq, nkv, scale, scale * LOG2E,
                dtb_error_word()};
   auto st = at::cuda::getCurrentCUDAStream();
   attn_bwd_dkdv_tc_kernel<HD><<<dim3(S / 128, nkv, B), 320, SmKV<HD>::TOTAL, st>>>(kv128, q64, do64, args);
   DTB_LAUNCH_CHECK();
-  attn_bwd_dq_tc_kernel<HD><<<dim3(S / 128, nq, B), 320, SmQ<HD>::TOTAL, st>>>(kv128, do128, q64, args);
+  if (dq_stages == 3)
+    attn_bwd_dq_tc_kernel<HD, 3><<<dim3(S / 128, nq, B), 320, SmQ<HD, 3>::TOTAL, st>>>(kv128, do128, q64, args);
+  else
+    attn_bwd_dq_tc_kernel<HD, 4><<<dim3(S / 128, nq, B), 320, SmQ<HD, 4>::TOTAL, st>>>(kv128, do128, q64, args);
   DTB_LAUNCH_CHECK();
 }
 

@@ -24,6 +24,9 @@ int64_t device_error();
 void gemm_peer_ar(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool b_mn, c10::optional<torch::Tensor> R,
                   c10::optional<torch::Tensor> alpha, std::vector<int64_t> bases, int64_t rank, int64_t stage_off,
                   int64_t flag_off, int64_t epoch, double timeout_s);
+void gemm_peer_rs(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool b_mn, c10::optional<torch::Tensor> R,
+                  std::vector<int64_t> bases, int64_t rank, int64_t stage_off, int64_t flag_off, int64_t epoch,
+                  double timeout_s, int64_t row0, int64_t rows);
 torch::Tensor sym_malloc(int64_t nbytes);
 torch::Tensor ipc_handle(torch::Tensor heap);
 int64_t ipc_open(torch::Tensor handle);
@@ -56,6 +59,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("S"), py::arg("nq"), py::arg("nkv"), py::arg("hd"), py::arg("scale"), py::arg("legacy") = false);
   m.def("device_error", &device_error, "read and clear the device error word");
   m.def("gemm_peer_ar", &gemm_peer_ar, "tcgen05 GEMM fused with an NVLink all-reduce over the peer group");
+  m.def("gemm_peer_rs", &gemm_peer_rs, "tcgen05 GEMM fused with an NVLink reduce-scatter of rows over the peer group");
   m.def("sym_malloc", &sym_malloc, "raw device allocation for a symmetric heap");
   m.def("ipc_handle", &ipc_handle);
   m.def("ipc_open", &ipc_open);

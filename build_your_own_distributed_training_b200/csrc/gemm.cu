@@ -68,6 +68,7 @@ struct GemmArgs {
   // EPI_PEER_AR: symmetric heaps of the group, staging area and flags inside them
   uint8_t* peer_base[MAX_PEERS];
   int peer_n, peer_rank;
+  int rs_row0, rs_rows;  // rs_rows > 0: reduce-scatter, this rank sums rows [rs_row0, rs_row0 + rs_rows) only
   long stage_off, flag_off;
   uint32_t epoch;
   uint64_t timeout_ns;
@@ -305,7 +306,7 @@ __device__ __forceinline__ void peer_sum_rows(const GemmArgs& a, int row0, int n
 #pragma unroll
     for (int i = 0; i < RU; ++i) {
       const int rr = row0 + r + i;
-      q[i] = (a.R != nullptr && rr < a.M) ? *reinterpret_cast<const uint4*>(a.R + (long)rr * a.ldr + n0 + c)
+      q[i] = (a.R != nullptr && rr < a.M) ? *reinterpret_cast<const uint4*>(a.R + (long)(rr - a.rs_row0) * a.ldr + n0 + c)
                                           : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
@@ -340,7 +341,7 @@ __device__ __forceinline__ void peer_sum_rows(const GemmArgs& a, int row0, int n
       o.y = pack_bf16x2(acc[2], acc[3]);
       o.z = pack_bf16x2(acc[4], acc[5]);
       o.w = pack_bf16x2(acc[6], acc[7]);
-      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.D) + (long)rr * a.ldd + n0 + c) = o;
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.D) + (long)(rr - a.rs_row0) * a.ldd + n0 + c) = o;
     }
   }
 }
@@ -351,6 +352,8 @@ __device__ __forceinline__ void peer_sum_rows(const GemmArgs& a, int row0, int n
 // order, so they agree bitwise.
 template <int BN>
 __device__ __forceinline__ bool peer_ar_finish(const GemmArgs& a, int tile, int mb, int nb, int quad, int lane) {
+  // reduce-scatter: tiles outside this rank's rows are summed by their owners
+  if (a.rs_rows > 0 && (mb * BM < a.rs_row0 || mb * BM >= a.rs_row0 + a.rs_rows)) return true;
   const int row = mb * BM + quad * 32 + lane;
   const int n0 = nb * BN;
   const long nflags = (long)a.flag_tiles * 4;
@@ -729,6 +732,7 @@ struct PeerCfg {
   long stage_off, flag_off;
   uint32_t epoch;
   double timeout_s;
+  int rs_row0 = 0, rs_rows = 0;  // reduce-scatter: this rank's output rows
 };
 
 static void gemm_impl(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_mn, bool b_mn, int64_t epi,
@@ -764,6 +768,12 @@ static void gemm_impl(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_
     g.flag_off = peer->flag_off;
     g.epoch = peer->epoch;
     g.timeout_ns = (uint64_t)(peer->timeout_s * 1e9);
+    g.rs_row0 = peer->rs_row0;
+    g.rs_rows = peer->rs_rows;
+    if (g.rs_rows > 0)
+      DTB_CHECK(g.rs_row0 % BM == 0 && g.rs_rows % BM == 0 && g.rs_row0 + g.rs_rows <= M && D.size(0) == g.rs_rows,
+                "peer GEMM reduce-scatter: row block [%d, %d) must be 128-row aligned and match D", g.rs_row0,
+                g.rs_row0 + g.rs_rows);
     DTB_CHECK(peer->stage_off % 16 == 0 && D.size(1) % 8 == 0, "peer GEMM: staging must be 16-byte aligned");
   } else {
     DTB_CHECK(epi != EPI_PEER_AR, "peer all-reduce epilogue needs a peer group");
@@ -818,7 +828,8 @@ static void gemm_impl(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_
   g.k_iters = (int)((K + BK - 1) / BK);
   g.num_tiles = g.m_blocks * g.n_blocks;
   g.flag_tiles = pair ? 2 * g.num_tiles : g.num_tiles;
-  TORCH_CHECK(D.size(0) == M && D.size(1) == g.N, "gemm: output shape mismatch");
+  TORCH_CHECK((g.rs_rows > 0 ? D.size(0) == g.rs_rows : D.size(0) == M) && D.size(1) == g.N,
+              "gemm: output shape mismatch");
   // tensor maps: A box = 128 rows (K-major) or 64 K-rows (MN-major); B likewise
   if (dtb_debug_enabled())
     fprintf(stderr, "[dtb] gemm M=%ld N=%d K=%ld a_mn=%d b_mn=%d epi=%d BN=%d A=%p B=%p D=%p alpha=%p\n", M, g.N, K,
@@ -859,4 +870,16 @@ void gemm_peer_ar(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool b_mn, 
                   int64_t flag_off, int64_t epoch, double timeout_s) {
   PeerCfg pc{bases, (int)rank, (long)stage_off, (long)flag_off, (uint32_t)epoch, timeout_s};
   gemm_impl(A, B, D, false, b_mn, dtb::EPI_PEER_AR, R, alpha, c10::nullopt, c10::nullopt, c10::nullopt, 0, 0, &pc);
+}
+
+// D = rows [row0, row0 + rows) of sum over the peer group of (A x B) (+ R, already
+// in the reduce-scattered layout): the GEMM fused with a reduce-scatter.  Every
+// rank stages its whole product; each rank sums only its own row block.
+void gemm_peer_rs(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool b_mn, c10::optional<torch::Tensor> R,
+                  std::vector<int64_t> bases, int64_t rank, int64_t stage_off, int64_t flag_off, int64_t epoch,
+                  double timeout_s, int64_t row0, int64_t rows) {
+  DTB_CHECK(rows > 0, "peer GEMM reduce-scatter: empty row block");
+  PeerCfg pc{bases, (int)rank, (long)stage_off, (long)flag_off, (uint32_t)epoch, timeout_s, (int)row0, (int)rows};
+  gemm_impl(A, B, D, false, b_mn, dtb::EPI_PEER_AR, R, c10::nullopt, c10::nullopt, c10::nullopt, c10::nullopt, 0, 0,
+            &pc);
 }

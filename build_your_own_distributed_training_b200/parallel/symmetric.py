@@ -200,6 +200,36 @@ class _RowParallelAR(torch.autograd.Function):
         return dx, dw, (dy if ctx.has_res else None), None, None
 
 
+class _RowParallelRS(torch.autograd.Function):
+    """Sequence parallel: ``y = reduce_scatter_rows(x @ W^T) + residual`` in one kernel.
+
+    Backward: the output gradient (this rank's rows) is all-gathered by pull,
+    then the input and weight gradients are plain GEMMs.
+    """
+
+    @staticmethod
+    def forward(ctx, x2, weight, residual, main_grad, comm):  # type: ignore[override]
+        out = comm.gemm_reduce_scatter(x2, weight, residual)
+        ctx.save_for_backward(x2, weight)
+        ctx.main_grad = main_grad
+        ctx.has_res = residual is not None
+        ctx.comm = comm
+        return out
+
+    @staticmethod
+    def backward(ctx, dy):  # type: ignore[override]
+        from ..ops import gemm
+        x2, w = ctx.saved_tensors
+        dy_full = ctx.comm.all_gather_rows(dy.contiguous())
+        dx = gemm.mm_nn(dy_full, w)
+        if ctx.main_grad is not None:
+            gemm.mm_tn_into_grad(dy_full, x2, ctx.main_grad, w.shape)
+            dw = None
+        else:
+            dw = gemm.mm_tn(dy_full, x2).to(w.dtype) if w.requires_grad else None
+        return dx, dw, (dy if ctx.has_res else None), None, None
+
+
 class TPComm:
     """Tensor-parallel collectives over NVLink for one TP group."""
 
@@ -256,9 +286,24 @@ class TPComm:
                               self.flag_off, self.calls, TIMEOUT_S)
         return out
 
+    # fused GEMM -> reduce-scatter of rows (+ residual in the scattered layout)
+    def gemm_reduce_scatter(self, x2: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None) -> torch.Tensor:
+        M, N = x2.shape[0], w.shape[0]
+        if M > self.max_tokens or N > self.width:
+            raise ValueError(f"row-parallel output [{M}, {N}] exceeds the TP staging area "
+                             f"[{self.max_tokens}, {self.width}]")
+        rows = M // self.size
+        out = torch.empty(rows, N, device=x2.device, dtype=torch.bfloat16)
+        off = self._slot()
+        native().gemm_peer_rs(x2, w, out, False, residual, self.heap.bases, self.rank, off, self.flag_off,
+                              self.calls, TIMEOUT_S, self.rank * rows, rows)
+        return out
+
     def row_parallel_linear(self, x2, weight, residual, main_grad):
-        from .tensor_parallel import _SeqReduceScatter, TPInfo  # noqa: F401
         if self._sequence_parallel:
+            rows = x2.shape[0] // self.size
+            if x2.shape[0] % self.size == 0 and rows % 128 == 0:
+                return _RowParallelRS.apply(x2.contiguous(), weight, residual, main_grad, self)
             from ..ops.linear import linear
             y = linear(x2, weight, main_grad=main_grad)
             y = _SeqReduceScatterPeer.apply(y, self)

@@ -71,6 +71,15 @@ def main():
         ys = [torch.empty_like(y) for _ in range(world)]
         dist.all_gather(ys, y)
         check(all(torch.equal(ys[0], t) for t in ys), "TP ranks disagree after the fused all-reduce")
+    # fused GEMM -> reduce-scatter of rows (sequence parallelism), residual in the scattered layout
+    rows = M // world
+    res_rs = torch.randn(rows, N, device=dev).to(torch.bfloat16)
+    for it in range(3):
+        y = tpc.gemm_reduce_scatter(x, w, res_rs)
+        part = gemm.mm_nt(x, w).float()
+        ref = torch.empty(rows, N, device=dev)
+        dist.reduce_scatter_tensor(ref, part)
+        check(rel(y, ref + res_rs.float()) < 1e-2, f"fused GEMM+reduce-scatter mismatch (call {it})")
     a = torch.randn(M, N, device=dev).to(torch.bfloat16)
     ar = tpc.all_reduce(a)
     ref_ar = a.float().clone()
@@ -94,7 +103,7 @@ def main():
     from build_your_own_distributed_training_b200.training.trainer import Trainer
     root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     results = {}
-    for tp in (world, 1):
+    for tp, sp in ((world, False), (world, True), (1, False)):
         ctx = build_process_context(tp, backend="nccl", verbose=False)
         for fused in (True, False):
             cfg = TrainingConfig.from_yaml(os.path.join(root, "config", "test_tiny.yaml"))
@@ -103,6 +112,7 @@ def main():
             cfg.model.max_seq_len = 256
             cfg.data.seq_len, cfg.data.micro_batch_size, cfg.data.dataset_path = 256, 2, "uniform"
             cfg.parallel.tp_size = tp
+            cfg.parallel.sequence_parallel = sp
             cfg.parallel.param_dtype = "bfloat16"
             cfg.backend = "nccl"
             cfg.kernels.fused_comm = fused
@@ -113,9 +123,9 @@ def main():
             for _ in range(3):
                 wdw, _ = tr._next_window()
                 losses.append(train_step(tr.model, wdw, tr.optimizer, tr.scheduler, ctx, cfg).loss)
-            results[(tp, fused)] = losses
-        lf, ln = results[(tp, True)], results[(tp, False)]
-        check(all(abs(p - q) < 2e-2 for p, q in zip(lf, ln)), f"tp={tp}: fused {lf} vs nccl {ln}")
+            results[(tp, sp, fused)] = losses
+        lf, ln = results[(tp, sp, True)], results[(tp, sp, False)]
+        check(all(abs(p - q) < 2e-2 for p, q in zip(lf, ln)), f"tp={tp} sp={sp}: fused {lf} vs nccl {ln}")
     torch.cuda.synchronize()
     check(native().device_error() == 0, "device error word set after training")
     if rank == 0:

@@ -121,6 +121,27 @@ def test_gemm_peer_allreduce_emulated_partner(M, N, K):
     assert int((heaps[1][flag_off:].view(torch.int32) == 7).sum()) > 0
 
 
+@pytest.mark.parametrize("M,N,K", [(1024, 768, 512), (4096, 4096, 2048)])
+def test_gemm_peer_reduce_scatter_emulated_partner(M, N, K):
+    """The fused GEMM + reduce-scatter of rows on one GPU, the partner emulated by memory:
+    rank 1 of 2 sums only its row block (the second half) and adds the scattered residual."""
+    a, b = _rand(M, K), _rand(N, K)
+    rows = M // 2
+    r = _rand(rows, N)
+    partner = _rand(M, N)
+    stage = M * N * 2
+    flag_off = (stage + 255) // 256 * 256
+    nflags = 2 * (M // 128 + 2) * (N // 128 + 2) * 4
+    heaps = [torch.zeros(flag_off + nflags * 4, device=DEV, dtype=torch.uint8) for _ in range(2)]
+    heaps[0][:stage].view(BF).copy_(partner.reshape(-1))   # rank 0's staged product
+    heaps[1][flag_off:].view(torch.int32).fill_(5)          # rank 0's flags, as seen by rank 1
+    out = torch.empty(rows, N, device=DEV, dtype=BF)
+    native().gemm_peer_rs(a, b, out, False, r, [h.data_ptr() for h in heaps], 1, 0, flag_off, 5, 1.0, rows, rows)
+    mine = (a.float() @ b.float().t()).to(BF).float()
+    ref = partner.float()[rows:] + mine[rows:] + r.float()
+    assert _rel(out, ref) < 1e-2
+
+
 def test_rmsnorm_fwd_bwd():
     from build_your_own_distributed_training_b200.ops.norm import rms_norm
     x = _rand(1000, 4096).requires_grad_()
