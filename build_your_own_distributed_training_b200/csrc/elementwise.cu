@@ -90,6 +90,141 @@ __global__ void __launch_bounds__(NT) rmsnorm_fwd_kernel(const __nv_bfloat16* __
   }
 }
 
+// 8 consecutive weights as fp32
+__device__ __forceinline__ void load_w8(const float* w, int c, float (&o)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(w + c), b = *reinterpret_cast<const float4*>(w + c + 4);
+  o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+}
+__device__ __forceinline__ void load_w8(const __nv_bfloat16* w, int c, float (&o)[8]) {
+  const uint4 q = *reinterpret_cast<const uint4*>(w + c);
+  const uint32_t* u = &q.x;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 f = unpack_bf16x2(u[k]);
+    o[2 * k] = f.x;
+    o[2 * k + 1] = f.y;
+  }
+}
+
+// Forward with the row in registers: two warps per row (4 rows per CTA);
+// thread t of a row holds its 16-byte vectors t, t+64, ..., so the row is read
+// once; the sum of squares is two warp reductions and one CTA barrier.
+// D = 512 * VPL.
+template <typename WT, int VPL>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_rows_kernel(const __nv_bfloat16* __restrict__ x,
+                                                               const WT* __restrict__ w,
+                                                               __nv_bfloat16* __restrict__ y,
+                                                               float* __restrict__ rstd, int M, float eps) {
+  constexpr int D = 512 * VPL;
+  __shared__ float wsum[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rl = warp >> 1;                      // row within the CTA
+  const int t = (warp & 1) * 32 + lane;          // thread within the row
+  const long row = (long)blockIdx.x * 4 + rl;
+  const bool valid = row < M;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * D);
+  uint4 q[VPL];
+  float ss = 0.f;
+  if (valid) {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      q[i] = xr[t + 64 * i];
+      const uint32_t* u = &q[i].x;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = unpack_bf16x2(u[k]);
+        ss += f.x * f.x + f.y * f.y;
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) wsum[warp] = ss;
+  __syncthreads();
+  if (!valid) return;
+  const float r = rsqrtf((wsum[2 * rl] + wsum[2 * rl + 1]) / (float)D + eps);
+  if (t == 0) rstd[row] = r;
+  uint4* yr = reinterpret_cast<uint4*>(y + row * D);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    float wv[8];
+    load_w8(w, (t + 64 * i) * 8, wv);
+    uint32_t* u = &q[i].x;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = unpack_bf16x2(u[k]);
+      u[k] = pack_bf16x2(f.x * r * wv[2 * k], f.y * r * wv[2 * k + 1]);
+    }
+    yr[t + 64 * i] = q[i];
+  }
+}
+
+// Backward with registers: thread t owns columns 8(t + 256j) .. +8 (j < VPT,
+// D = 2048 * VPT); the weights and the dw partial sums stay in registers for
+// all the CTA's rows and each row of x and dy is read once.  Same arithmetic
+// and row order as rmsnorm_bwd_kernel, so the dw partials are identical.
+template <typename WT, int VPT>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_rows_kernel(const __nv_bfloat16* __restrict__ dy,
+                                                               const __nv_bfloat16* __restrict__ x,
+                                                               const WT* __restrict__ w,
+                                                               const float* __restrict__ rstd,
+                                                               __nv_bfloat16* __restrict__ dx, float* __restrict__ part,
+                                                               int M, int rows_per_cta) {
+  constexpr int D = 2048 * VPT;
+  __shared__ float red[32];
+  const int t = threadIdx.x;
+  float wv[VPT][8], dw[VPT][8];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    load_w8(w, (t + 256 * j) * 8, wv[j]);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) dw[j][k] = 0.f;
+  }
+  const int r0 = blockIdx.x * rows_per_cta;
+  const int r1 = min(M, r0 + rows_per_cta);
+  for (int row = r0; row < r1; ++row) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (long)row * D);
+    const uint4* gr = reinterpret_cast<const uint4*>(dy + (long)row * D);
+    uint4 qx[VPT], qg[VPT];
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      qx[j] = xr[t + 256 * j];
+      qg[j] = gr[t + 256 * j];
+    }
+    const float rs = rstd[row];
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const uint32_t *ux = &qx[j].x, *ug = &qg[j].x;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 fx = unpack_bf16x2(ux[k]), fg = unpack_bf16x2(ug[k]);
+        dot += fg.x * wv[j][2 * k] * fx.x * rs + fg.y * wv[j][2 * k + 1] * fx.y * rs;
+      }
+    }
+    const float mean = block_sum<256>(dot, red) / (float)D;
+    uint4* dr = reinterpret_cast<uint4*>(dx + (long)row * D);
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const uint32_t *ux = &qx[j].x, *ug = &qg[j].x;
+      uint4 qo;
+      uint32_t* uo = &qo.x;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 fx = unpack_bf16x2(ux[k]), fg = unpack_bf16x2(ug[k]);
+        const float xh0 = fx.x * rs, xh1 = fx.y * rs;
+        uo[k] = pack_bf16x2(rs * (fg.x * wv[j][2 * k] - xh0 * mean), rs * (fg.y * wv[j][2 * k + 1] - xh1 * mean));
+        dw[j][2 * k] += fg.x * xh0;
+        dw[j][2 * k + 1] += fg.y * xh1;
+      }
+      dr[t + 256 * j] = qo;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < VPT; ++j)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) part[(long)blockIdx.x * D + (t + 256 * j) * 8 + k] = dw[j][k];
+}
+
 // dx = rstd * (g*w - xhat * mean(g*w*xhat)); per-CTA partial of sum(g*xhat)
 // over its rows written to part[blockIdx.x, :].
 template <typename WT, int NT>
@@ -399,6 +534,39 @@ using namespace dtb;
 
 static cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream(); }
 
+// The register-resident forward for the usual widths (512 ... 8192); false
+// when D needs the general kernel.
+template <typename WT>
+static bool rmsnorm_fwd_rows_t(const __nv_bfloat16* x, const WT* w, __nv_bfloat16* y, float* rstd, int M, int D,
+                               float eps) {
+  const dim3 grid((M + 3) / 4);
+  auto st = cur_stream();
+  switch (D) {
+    case 512: rmsnorm_fwd_rows_kernel<WT, 1><<<grid, 256, 0, st>>>(x, w, y, rstd, M, eps); return true;
+    case 1024: rmsnorm_fwd_rows_kernel<WT, 2><<<grid, 256, 0, st>>>(x, w, y, rstd, M, eps); return true;
+    case 2048: rmsnorm_fwd_rows_kernel<WT, 4><<<grid, 256, 0, st>>>(x, w, y, rstd, M, eps); return true;
+    case 3072: rmsnorm_fwd_rows_kernel<WT, 6><<<grid, 256, 0, st>>>(x, w, y, rstd, M, eps); return true;
+    case 4096: rmsnorm_fwd_rows_kernel<WT, 8><<<grid, 256, 0, st>>>(x, w, y, rstd, M, eps); return true;
+    case 5120: rmsnorm_fwd_rows_kernel<WT, 10><<<grid, 256, 0, st>>>(x, w, y, rstd, M, eps); return true;
+    case 8192: rmsnorm_fwd_rows_kernel<WT, 16><<<grid, 256, 0, st>>>(x, w, y, rstd, M, eps); return true;
+    default: return false;
+  }
+}
+
+static bool rmsnorm_fwd_rows(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& y, torch::Tensor& rstd,
+                             int M, int D, float eps) {
+  auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  auto yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  bool done;
+  if (w.scalar_type() == at::kFloat)
+    done = rmsnorm_fwd_rows_t(xp, w.data_ptr<float>(), yp, rstd.data_ptr<float>(), M, D, eps);
+  else
+    done = rmsnorm_fwd_rows_t(xp, reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), yp, rstd.data_ptr<float>(), M,
+                              D, eps);
+  if (done) DTB_LAUNCH_CHECK();
+  return done;
+}
+
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.is_contiguous(), "rmsnorm: bf16 [M,D]");
   const c10::cuda::CUDAGuard g(x.device());
@@ -407,6 +575,7 @@ std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double 
   auto y = torch::empty_like(x);
   auto rstd = torch::empty({M}, x.options().dtype(at::kFloat));
   if (M == 0) return {y, rstd};
+  if (rmsnorm_fwd_rows(x, w, y, rstd, M, D, (float)eps)) return {y, rstd};
   if (w.scalar_type() == at::kFloat)
     rmsnorm_fwd_kernel<float, 256><<<M, 256, 0, cur_stream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), w.data_ptr<float>(),
@@ -426,6 +595,22 @@ void rmsnorm_bwd_launch(const __nv_bfloat16* dy, const __nv_bfloat16* x, const v
                         int rows_per_cta, cudaStream_t st) {
   const int nb = (M + rows_per_cta - 1) / rows_per_cta;
   const size_t sh = (size_t)D * sizeof(float);
+  const int vpt = D % 2048 == 0 ? D / 2048 : 0;
+  if (vpt >= 1 && vpt <= 4) {
+    // register-resident variant: same partials, one read of x and dy
+#define DTB_RMS_BWD_ROWS(WT, V)                                                                                   \
+  rmsnorm_bwd_rows_kernel<WT, V><<<nb, 256, 0, st>>>(dy, x, (const WT*)w, rstd, dx, part, M, rows_per_cta)
+    if (w_f32) {
+      if (vpt == 1) DTB_RMS_BWD_ROWS(float, 1); else if (vpt == 2) DTB_RMS_BWD_ROWS(float, 2);
+      else if (vpt == 3) DTB_RMS_BWD_ROWS(float, 3); else DTB_RMS_BWD_ROWS(float, 4);
+    } else {
+      if (vpt == 1) DTB_RMS_BWD_ROWS(__nv_bfloat16, 1); else if (vpt == 2) DTB_RMS_BWD_ROWS(__nv_bfloat16, 2);
+      else if (vpt == 3) DTB_RMS_BWD_ROWS(__nv_bfloat16, 3); else DTB_RMS_BWD_ROWS(__nv_bfloat16, 4);
+    }
+#undef DTB_RMS_BWD_ROWS
+    reduce_partials_kernel<<<(D + 31) / 32, 256, 0, st>>>(part, dw_acc, nb, D);
+    return;
+  }
   if (w_f32)
     rmsnorm_bwd_kernel<float, 256><<<nb, 256, sh, st>>>(dy, x, (const float*)w, rstd, dx, part, M, D, rows_per_cta);
   else

@@ -142,10 +142,13 @@ def test_gemm_peer_reduce_scatter_emulated_partner(M, N, K):
     assert _rel(out, ref) < 1e-2
 
 
-def test_rmsnorm_fwd_bwd():
+@pytest.mark.parametrize("M,D,wdt", [(1000, 4096, BF), (1001, 2048, torch.float32), (333, 1536, BF),
+                                     (64, 8192, BF)])
+def test_rmsnorm_fwd_bwd(M, D, wdt):
+    """Register-resident kernels for the usual widths, the general kernels otherwise (D = 1536)."""
     from build_your_own_distributed_training_b200.ops.norm import rms_norm
-    x = _rand(1000, 4096).requires_grad_()
-    w = (1 + 0.1 * torch.randn(4096, device=DEV)).to(BF).requires_grad_()
+    x = _rand(M, D).requires_grad_()
+    w = (1 + 0.1 * torch.randn(D, device=DEV)).to(wdt).requires_grad_()
     y = rms_norm(x, w, 1e-5)
     xr = x.detach().float().requires_grad_()
     wr = w.detach().float().requires_grad_()
