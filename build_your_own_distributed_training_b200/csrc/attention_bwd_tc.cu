@@ -79,7 +79,13 @@ struct BwdArgs {
   int S, nq, nkv;
   float scale, scale_log2;
   int* err;
+  long long* trace;   // phase timestamps of one CTA (DTB_ATTN_TRACE=1), else nullptr
 };
+
+// clock64 timestamp of phase k of iteration j for trace row `role`
+__device__ __forceinline__ void trace_mark(const BwdArgs& a, bool on, int role, int j, int k) {
+  if (on && j < 64) a.trace[(role * 64 + j) * 8 + k] = clock64();
+}
 
 // ============================================================== dK / dV
 template <int HD>
@@ -371,6 +377,7 @@ __global__ void __launch_bounds__(320, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool tr = a.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
   const int nqb = a.S / BQ;
   const int qb = nqb - 1 - blockIdx.x;
   const int h = blockIdx.y, b = blockIdx.z;
@@ -415,10 +422,12 @@ __global__ void __launch_bounds__(320, 1)
       }
       for (int j = 0; j < nkt; ++j) {
         const int st = j % NS;
+        trace_mark(a, tr, 0, j, 0);
         if (*abort_flag || !mbar_wait(&kv_empty[st], ((j / NS) & 1) ^ 1, a.err)) {
           *abort_flag = 1;
           break;
         }
+        trace_mark(a, tr, 0, j, 1);
         mbar_arrive_expect_tx(&kv_full[st], 2 * L::KT);
 #pragma unroll
         for (int c = 0; c < HD / 64; ++c) {
@@ -437,8 +446,11 @@ __global__ void __launch_bounds__(320, 1)
       bool ok = mbar_wait(q_full, 0, a.err);
       auto issue_s = [&](int j) -> bool {
         const int st = j % NS, tb = j & 1;
+        trace_mark(a, tr, 1, j, 0);
         if (!mbar_wait(&kv_full[st], (j / NS) & 1, a.err)) return false;
+        trace_mark(a, tr, 1, j, 1);
         if (!mbar_wait(&s_empty[tb], ((j >> 1) & 1) ^ 1, a.err)) return false;
+        trace_mark(a, tr, 1, j, 2);
         tc_fence_after();
         const uint32_t k0 = smem_u32(sm + L::K_OFF + st * L::KT), v0 = smem_u32(sm + L::V_OFF + st * L::KT);
 #pragma unroll
@@ -455,6 +467,7 @@ __global__ void __launch_bounds__(320, 1)
       if (ok && nkt > 1) ok = issue_s(1);
       for (int j = 0; j < nkt && ok && !*abort_flag; ++j) {
         const int pb = j & 1;
+        trace_mark(a, tr, 2, j, 0);
         if (!mbar_wait(&p_full[pb], (j >> 1) & 1, a.err)) {
           ok = false;
           break;
@@ -469,6 +482,7 @@ __global__ void __launch_bounds__(320, 1)
                     (j | kk) != 0);
         umma_commit(&kv_empty[st]);
         umma_commit(&p_done[pb]);
+        trace_mark(a, tr, 2, j, 1);
         if (j + 2 < nkt && !issue_s(j + 2)) {
           ok = false;
           break;
@@ -488,6 +502,8 @@ __global__ void __launch_bounds__(320, 1)
     bool ok = true;
     for (int j = 0; j < nkt; ++j) {
       const int tb = j & 1;
+      const bool trw = tr && warp == 2 && lane == 0;
+      trace_mark(a, trw, 3, j, 0);
       if (*abort_flag || !mbar_wait(&s_full[tb], (j >> 1) & 1, a.err)) {
         ok = false;
         break;
@@ -496,9 +512,11 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t sr[32], dr[32];
       tmem_ld32_async(t_s[tb] + lo + c0, sr);
       tmem_ld32_async(t_dp[tb] + lo + c0, dr);
+      trace_mark(a, trw, 3, j, 1);
       tmem_wait_ld();
       tmem_regs(sr);
       tmem_regs(dr);
+      trace_mark(a, trw, 3, j, 2);
       tc_fence_before();
       mbar_arrive(&s_empty[tb]);
       // key tiles that reach past the first query row of this tile hold masked columns
@@ -516,6 +534,7 @@ __global__ void __launch_bounds__(320, 1)
         }
         pd[c / 2] = pack_bf16x2(d[0], d[1]);
       }
+      trace_mark(a, trw, 3, j, 3);
       // buffer j & 1 was last read by the dQ MMAs of key tile j - 2
       if (j > 1) {
         if (!mbar_wait(&p_done[j & 1], ((j - 2) >> 1) & 1, a.err)) {
@@ -523,11 +542,265 @@ __global__ void __launch_bounds__(320, 1)
           break;
         }
       }
+      trace_mark(a, trw, 3, j, 4);
       store_row32(sm + L::DS_OFF + (j & 1) * 16384, r, half, pd);
       fence_proxy_async_smem();
       mbar_arrive(&p_full[j & 1]);
+      trace_mark(a, trw, 3, j, 5);
     }
     if (ok && mbar_wait(&p_done[(nkt - 1) & 1], ((nkt - 1) >> 1) & 1, a.err)) {
+      tc_fence_after();
+      const long ld = (long)(a.nq + 2 * a.nkv) * HD;
+      __nv_bfloat16* gq = a.dqkv + ((long)row0 + qr) * ld + h * HD;
+#pragma unroll 1
+      for (int c = half * (HD / 2); c < (half + 1) * (HD / 2); c += 32) {
+        float dq[32];
+        tmem_ld32(t_dq + lo + c, dq);
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 w;
+          w.x = pack_bf16x2(dq[i] * a.scale, dq[i + 1] * a.scale);
+          w.y = pack_bf16x2(dq[i + 2] * a.scale, dq[i + 3] * a.scale);
+          w.z = pack_bf16x2(dq[i + 4] * a.scale, dq[i + 5] * a.scale);
+          w.w = pack_bf16x2(dq[i + 6] * a.scale, dq[i + 7] * a.scale);
+          *reinterpret_cast<uint4*>(gq + c + i) = w;
+        }
+      }
+    } else {
+      *abort_flag = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// ============================================================== dQ, 128-key tiles
+// Same product as attn_bwd_dq_tc_kernel with 128-key tiles: S, dP and dQ are
+// M=128 x N=128 MMAs, so each tcgen05.mma carries twice the work of the
+// 64-key version and the MMA count per key drops by 40% (that kernel is bound
+// by the cost of issuing its small N=64 instructions).  TMEM holds one S and
+// one dP (128 columns each) plus dQ; S_{j+1} is issued as soon as the
+// elementwise warps have read S_j, so it overlaps their math and dQ_j.
+template <int HD>
+struct SmQ128 {
+  static constexpr int QT = 128 * HD * 2;        // Q or dO: [hd/64][128][128 B]
+  static constexpr int KT = 128 * HD * 2;        // K or V: [hd/64][128 keys][128 B]
+  // separate rings: a K stage is held until dQ_j finishes, a V stage only until
+  // dP_j does, so K gets the depth
+  static constexpr int NSK = 3;
+  static constexpr int NSV = HD == 128 ? 1 : 2;
+  static constexpr int Q_OFF = 0;
+  static constexpr int O_OFF = Q_OFF + QT;
+  static constexpr int K_OFF = O_OFF + QT;
+  static constexpr int V_OFF = K_OFF + NSK * KT;
+  static constexpr int DS_OFF = V_OFF + NSV * KT;  // dS [128 q][128 keys] bf16: 2 atoms
+  static constexpr int BAR_OFF = DS_OFF + 32768;
+  static constexpr int N_BARS = 2 * (NSK + NSV) + 6;
+  static constexpr int TOTAL = BAR_OFF + N_BARS * 8 + 16 + 1024;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(320, 1)
+    attn_bwd_dq128_tc_kernel(const __grid_constant__ CUtensorMap tm_q128, const __grid_constant__ CUtensorMap tm_do128,
+                             const __grid_constant__ CUtensorMap tm_kv128, const BwdArgs a) {
+  using L = SmQ128<HD>;
+  constexpr int BQ = 128, BKV = 128, NSK = L::NSK, NSV = L::NSV;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;                   // [NSK]
+  uint64_t* k_empty = k_full + NSK;              // [NSK]
+  uint64_t* v_full = k_empty + NSK;              // [NSV]
+  uint64_t* v_empty = v_full + NSV;              // [NSV]
+  uint64_t* s_full = v_empty + NSV;              // S_j and dP_j in TMEM
+  uint64_t* s_empty = s_full + 1;                // the elementwise warps have read S_j and dP_j
+  uint64_t* p_full = s_full + 2;                 // dS_j in shared memory
+  uint64_t* p_done = s_full + 3;                 // the dQ MMAs of key tile j (read dS) finished
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + L::N_BARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool tr = a.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+  const int nqb = a.S / BQ;
+  const int qb = nqb - 1 - blockIdx.x;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (a.nq / a.nkv);
+  const int q0 = qb * BQ;
+  const int nkt = qb + 1;                 // causal: key tiles 0..qb
+  const int row0 = b * a.S;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < NSK; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < NSV; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_empty, 256);
+    mbar_init(p_full, 256);
+    mbar_init(p_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const uint32_t t_s = tmem, t_dp = tmem + 128, t_dq = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, 2 * L::QT);
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c) {
+        tma_load_2d(sm + L::Q_OFF + c * 16384, &tm_q128, q_full, h * HD + c * 64, row0 + q0);
+        tma_load_2d(sm + L::O_OFF + c * 16384, &tm_do128, q_full, h * HD + c * 64, row0 + q0);
+      }
+      for (int j = 0; j < nkt; ++j) {
+        const int sk = j % NSK, sv = j % NSV;
+        trace_mark(a, tr, 0, j, 0);
+        if (*abort_flag || !mbar_wait(&k_empty[sk], ((j / NSK) & 1) ^ 1, a.err)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&k_full[sk], L::KT);
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c)
+          tma_load_2d(sm + L::K_OFF + sk * L::KT + c * 16384, &tm_kv128, &k_full[sk], (a.nq + hk) * HD + c * 64,
+                      row0 + j * BKV);
+        trace_mark(a, tr, 0, j, 1);
+        if (*abort_flag || !mbar_wait(&v_empty[sv], ((j / NSV) & 1) ^ 1, a.err)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[sv], L::KT);
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c)
+          tma_load_2d(sm + L::V_OFF + sv * L::KT + c * 16384, &tm_kv128, &v_full[sv],
+                      (a.nq + a.nkv + hk) * HD + c * 64, row0 + j * BKV);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_S = idesc_bf16(128, BKV, false, false);  // S = Q K^T, dP = dO V^T
+      constexpr uint32_t ID_Q = idesc_bf16(128, HD, false, true);    // dQ += dS K (K tile MN-major)
+      const uint32_t qa = smem_u32(sm + L::Q_OFF), oa = smem_u32(sm + L::O_OFF), dsa = smem_u32(sm + L::DS_OFF);
+      bool ok = mbar_wait(q_full, 0, a.err);
+      auto issue_s = [&](int j) -> bool {
+        const int sk = j % NSK, sv = j % NSV;
+        trace_mark(a, tr, 1, j, 0);
+        if (!mbar_wait(&k_full[sk], (j / NSK) & 1, a.err)) return false;
+        if (!mbar_wait(&v_full[sv], (j / NSV) & 1, a.err)) return false;
+        trace_mark(a, tr, 1, j, 1);
+        // TMEM S / dP are free once the elementwise warps read S_{j-1}, dP_{j-1}
+        if (j > 0 && !mbar_wait(s_empty, (j - 1) & 1, a.err)) return false;
+        trace_mark(a, tr, 1, j, 2);
+        tc_fence_after();
+        const uint32_t k0 = smem_u32(sm + L::K_OFF + sk * L::KT), v0 = smem_u32(sm + L::V_OFF + sv * L::KT);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t o = (kk >> 2) * 16384 + (kk & 3) * 32;   // 128-row atoms on both sides
+          umma_bf16(t_s, sdesc_sw128(qa + o, 16, 1024), sdesc_sw128(k0 + o, 16, 1024), ID_S, kk != 0);
+          umma_bf16(t_dp, sdesc_sw128(oa + o, 16, 1024), sdesc_sw128(v0 + o, 16, 1024), ID_S, kk != 0);
+        }
+        umma_commit(s_full);
+        umma_commit(&v_empty[sv]);  // V_j is only read by dP_j
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < nkt && ok && !*abort_flag; ++j) {
+        if (j + 1 < nkt && !issue_s(j + 1)) {
+          ok = false;
+          break;
+        }
+        trace_mark(a, tr, 2, j, 0);
+        if (!mbar_wait(p_full, j & 1, a.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int sk = j % NSK;
+        const uint32_t k0 = smem_u32(sm + L::K_OFF + sk * L::KT);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk)
+          umma_bf16(t_dq, sdesc_sw128(dsa + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                    sdesc_sw128(k0 + kk * 2048, 16384, 1024), ID_Q, (j | kk) != 0);
+        umma_commit(&k_empty[sk]);
+        umma_commit(p_done);
+        trace_mark(a, tr, 2, j, 1);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;  // warpgroup: key columns [64*half, 64*half + 64)
+    const int c0 = half * 64;
+    const int r = quad * 32 + lane;
+    const int qr = q0 + r;
+    const uint32_t lo = (uint32_t)(quad * 32) << 16;
+    const long li = ((long)b * a.nq + h) * a.S + qr;
+    const float L2 = a.lse[li] * LOG2E, Dr = a.Dv[li];
+    bool ok = true;
+    for (int j = 0; j < nkt; ++j) {
+      const bool trw = tr && warp == 2 && lane == 0;
+      trace_mark(a, trw, 3, j, 0);
+      if (*abort_flag || !mbar_wait(s_full, j & 1, a.err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      trace_mark(a, trw, 3, j, 1);
+      // S first; the dP loads then overlap the exponentials
+      uint32_t sr[2][32], dr[2][32];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) tmem_ld32_async(t_s + lo + c0 + 32 * i, sr[i]);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 2; ++i) tmem_regs(sr[i]);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) tmem_ld32_async(t_dp + lo + c0 + 32 * i, dr[i]);
+      const bool diag = j == nkt - 1;  // the last key tile is the diagonal one
+      float p[64];
+#pragma unroll
+      for (int cc = 0; cc < 64; ++cc) {
+        p[cc] = ex2_approx(fmaf(__uint_as_float(sr[cc >> 5][cc & 31]), a.scale_log2, -L2));
+        if (diag && j * BKV + c0 + cc > qr) p[cc] = 0.f;
+      }
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 2; ++i) tmem_regs(dr[i]);
+      trace_mark(a, trw, 3, j, 2);
+      tc_fence_before();
+      mbar_arrive(s_empty);
+      uint32_t pd[32];
+#pragma unroll
+      for (int c = 0; c < 64; c += 2)
+        pd[c / 2] = pack_bf16x2(p[c] * (__uint_as_float(dr[c >> 5][c & 31]) - Dr),
+                                p[c + 1] * (__uint_as_float(dr[(c + 1) >> 5][(c + 1) & 31]) - Dr));
+      trace_mark(a, trw, 3, j, 3);
+      // the dS buffer was last read by the dQ MMAs of key tile j - 1
+      if (j > 0 && !mbar_wait(p_done, (j - 1) & 1, a.err)) {
+        ok = false;
+        break;
+      }
+      trace_mark(a, trw, 3, j, 4);
+      store_row64(sm + L::DS_OFF + half * 16384, r, pd);
+      fence_proxy_async_smem();
+      mbar_arrive(p_full);
+      trace_mark(a, trw, 3, j, 5);
+    }
+    if (ok && mbar_wait(p_done, (nkt - 1) & 1, a.err)) {
       tc_fence_after();
       const long ld = (long)(a.nq + 2 * a.nkv) * HD;
       __nv_bfloat16* gq = a.dqkv + ((long)row0 + qr) * ld + h * HD;
@@ -601,23 +874,54 @@ void bwd_tc_launch(const torch::Tensor& qkv, const torch::Tensor& dO, const floa
                                   SmQ<HD, 3>::TOTAL));
     DTB_CUDA(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<HD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   SmQ<HD, 4>::TOTAL));
+    DTB_CUDA(cudaFuncSetAttribute(attn_bwd_dq128_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  SmQ128<HD>::TOTAL));
     cfg = true;
   }
+  // dQ key tile: 128 unless DTB_ATTN_DQ_BKV=64
+  static const bool dq128 = [] {
+    const char* e = getenv("DTB_ATTN_DQ_BKV");
+    return !(e != nullptr && e[0] == '6');
+  }();
   // K/V ring depth of the dQ kernel: 4 unless DTB_ATTN_DQ_STAGES=3
   static const int dq_stages = [] {
     const char* e = getenv("DTB_ATTN_DQ_STAGES");
     return (e != nullptr && e[0] == '3') ? 3 : 4;
   }();
+  static const bool trace_on = [] {
+    const char* e = getenv("DTB_ATTN_TRACE");
+    return e != nullptr && e[0] == '1';
+  }();
+  torch::Tensor trace;
+  if (trace_on) trace = torch::zeros({4 * 64 * 8}, qkv.options().dtype(at::kLong));
   BwdArgs args{lse, Dv, reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), S, nq, nkv, scale, scale * LOG2E,
-               dtb_error_word()};
+               dtb_error_word(), trace_on ? reinterpret_cast<long long*>(trace.data_ptr<int64_t>()) : nullptr};
   auto st = at::cuda::getCurrentCUDAStream();
   attn_bwd_dkdv_tc_kernel<HD><<<dim3(S / 128, nkv, B), 320, SmKV<HD>::TOTAL, st>>>(kv128, q64, do64, args);
   DTB_LAUNCH_CHECK();
-  if (dq_stages == 3)
+  if (dq128)
+    attn_bwd_dq128_tc_kernel<HD><<<dim3(S / 128, nq, B), 320, SmQ128<HD>::TOTAL, st>>>(kv128, do128, kv128, args);
+  else if (dq_stages == 3)
     attn_bwd_dq_tc_kernel<HD, 3><<<dim3(S / 128, nq, B), 320, SmQ<HD, 3>::TOTAL, st>>>(kv128, do128, q64, args);
   else
     attn_bwd_dq_tc_kernel<HD, 4><<<dim3(S / 128, nq, B), 320, SmQ<HD, 4>::TOTAL, st>>>(kv128, do128, q64, args);
   DTB_LAUNCH_CHECK();
+  if (trace_on) {
+    // diagnostic: per-iteration phase times (SM cycles) of the dQ kernel's first CTA
+    auto h = trace.cpu();
+    const int64_t* t = h.data_ptr<int64_t>();
+    const int64_t t0 = t[(1 * 64 + 0) * 8 + 0];
+    fprintf(stderr, "[dtb] dQ trace (cycles from the first S issue): producer(empty,issue) "
+                    "mma(kvwait,kvdone,sempty | pwait,pdone) elementwise(start,sfull,ldissued,lddone,computed,stored)\n");
+    for (int j = 0; j < 64; ++j) {
+      auto v = [&](int role, int k) { const int64_t x = t[(role * 64 + j) * 8 + k]; return x ? x - t0 : -1; };
+      if (!t[(3 * 64 + j) * 8 + 0]) break;
+      fprintf(stderr, "[dtb] j=%2d P %7lld %7lld | S %7lld %7lld %7lld | G %7lld %7lld | E %7lld %7lld %7lld %7lld %7lld %7lld\n", j,
+              (long long)v(0, 0), (long long)v(0, 1), (long long)v(1, 0), (long long)v(1, 1), (long long)v(1, 2),
+              (long long)v(2, 0), (long long)v(2, 1), (long long)v(3, 0), (long long)v(3, 1), (long long)v(3, 2),
+              (long long)v(3, 3), (long long)v(3, 4), (long long)v(3, 5));
+    }
+  }
 }
 
 }  // namespace fab
