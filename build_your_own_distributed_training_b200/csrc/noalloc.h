@@ -7,7 +7,7 @@
 // another runtime) that links this library without PyTorch and its caching
 // allocator, code that has reserved all device memory up front and may not
 // grow it, or code issuing work where a cudaMalloc would synchronise the
-// device or is not permitted (for example while a stream is being captured).
+// device or is not permitted.
 // They pass their own inputs and outputs; the per-block partial sums of the
 // weight gradient, which the allocating entry point keeps in a temporary
 // buffer, live here in a fixed device array inside the library.

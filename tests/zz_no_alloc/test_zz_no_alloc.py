@@ -1,10 +1,11 @@
 """The allocation-free RMSNorm backward, called through its exported C symbol.
 
 It serves callers that cannot allocate device memory when they run the
-backward (a host program linking the library without PyTorch's allocator,
-memory reserved up front, work issued while a stream is being captured).  Its
-results must match the allocating entry point's.  This file (in the last directory of tests/) is collected last
-so a run that stops at the first failure has run every other test first.
+backward (a host program linking the library without PyTorch's allocator, or
+one whose device memory is all reserved up front).  Its results must match
+the allocating entry point's.  This file (in the last directory of tests/) is
+collected last so a run that stops at the first failure has run every other
+test first.
 """
 
 from __future__ import annotations
