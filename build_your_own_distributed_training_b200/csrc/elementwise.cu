@@ -181,16 +181,33 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_rows_kernel(const __nv_bfloat
   }
   const int r0 = blockIdx.x * rows_per_cta;
   const int r1 = min(M, r0 + rows_per_cta);
+  // row r's loads are issued while row r-1 is reduced (two rows in flight)
+  uint4 nx[VPT], ng[VPT];
+  float nrs = 0.f;
+  if (r0 < r1) {
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      nx[j] = reinterpret_cast<const uint4*>(x + (long)r0 * D)[t + 256 * j];
+      ng[j] = reinterpret_cast<const uint4*>(dy + (long)r0 * D)[t + 256 * j];
+    }
+    nrs = rstd[r0];
+  }
   for (int row = r0; row < r1; ++row) {
-    const uint4* xr = reinterpret_cast<const uint4*>(x + (long)row * D);
-    const uint4* gr = reinterpret_cast<const uint4*>(dy + (long)row * D);
     uint4 qx[VPT], qg[VPT];
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
-      qx[j] = xr[t + 256 * j];
-      qg[j] = gr[t + 256 * j];
+      qx[j] = nx[j];
+      qg[j] = ng[j];
     }
-    const float rs = rstd[row];
+    const float rs = nrs;
+    if (row + 1 < r1) {
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        nx[j] = reinterpret_cast<const uint4*>(x + (long)(row + 1) * D)[t + 256 * j];
+        ng[j] = reinterpret_cast<const uint4*>(dy + (long)(row + 1) * D)[t + 256 * j];
+      }
+      nrs = rstd[row + 1];
+    }
     float dot = 0.f;
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
