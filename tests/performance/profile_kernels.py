@@ -102,6 +102,26 @@ def case_gemm_peer_ar():
     return run, 2 * T * D * (D // 2), 0
 
 
+def case_gemm_peer_rs():
+    # tp=2 sequence-parallel output projection: [T, D/2] x [D, D/2]^T, reduce-scattered to rank 1's rows
+    a, b = _bf(T, D // 2), _bf(D, D // 2)
+    rows = T // 2
+    r = _bf(rows, D)
+    out = torch.empty(rows, D, device=DEV, dtype=BF)
+    stage = T * D * 2
+    flag_off = (stage + 255) // 256 * 256
+    nflags = 2 * (T // 128 + 2) * (D // 128 + 2) * 4
+    heaps, bases = _emulated_heaps(2, flag_off + nflags * 4)
+    heaps[0][:stage].view(BF).copy_(_bf(T * D))       # rank 0's staged product
+    epoch = [0]
+
+    def run():
+        epoch[0] += 1
+        heaps[1][flag_off:].view(torch.int32).fill_(epoch[0])    # rank 0's flags already published
+        native().gemm_peer_rs(a, b, out, False, r, bases, 1, 0, flag_off, epoch[0], 1.0, rows, rows)
+    return run, 2 * T * D * (D // 2), 0
+
+
 def case_peer_all_gather():
     shard = 128 << 20
     heaps, bases = _emulated_heaps(2, shard)
