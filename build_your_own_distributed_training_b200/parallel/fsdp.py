@@ -312,11 +312,16 @@ class FullyShardedModel(nn.Module):
             self._bwd_started = True
             torch.autograd.Variable._execution_engine.queue_callback(self._finish_backward)
         self._ensure(bi)
-        if bi - 1 >= 0:
+        # BACKWARD_PRE: gather the previous block while this one computes its gradients
+        if bi - 1 >= 0 and self.cfg.backward_prefetch == "BACKWARD_PRE":
             self._prefetch(bi - 1)
 
     def _post_backward(self, bi: int) -> None:
         nvtx.pop()
+        # BACKWARD_POST: gather the previous block once this one's gradients are done
+        # (less overlap, one gathered block fewer alive during the gradient GEMMs)
+        if bi - 1 >= 0 and self.cfg.backward_prefetch == "BACKWARD_POST":
+            self._prefetch(bi - 1)
         u = self.units[bi]
         if self._sync:
             self._reduce_scatter(u)

@@ -148,3 +148,32 @@ def _memory_bound_worker(rank, world, limit):
 def test_gathered_blocks_are_bounded(limit):
     """At most two (limit_all_gathers) or three gathered blocks exist at any time."""
     run_distributed(_memory_bound_worker, 2, limit)
+
+
+def _prefetch_order_worker(rank, world, mode, out):
+    cfg = tiny_config(parallel__sharding_strategy="FULL_SHARD", parallel__backward_prefetch=mode,
+                      model__n_layers=3)
+    ctx = build_process_context(1, backend="gloo", verbose=False)
+    eng = build_engine(cfg, ctx)
+    events = []
+    orig_post = eng._post_backward
+    eng._prefetch = lambda bi: events.append(("prefetch", bi))
+
+    def post(bi):
+        events.append(("post", bi))
+        orig_post(bi)
+    eng._post_backward = post
+    _, loss = eng(torch.randint(0, 256, (2, 16)), labels=torch.randint(0, 256, (2, 16)))
+    events.clear()  # keep the backward only
+    loss.backward()
+    out.extend(events)
+
+
+@pytest.mark.parametrize("mode", ["BACKWARD_PRE", "BACKWARD_POST"])
+def test_backward_prefetch_order(single_process_pg, mode):
+    """BACKWARD_PRE gathers block i-1 when block i's backward starts; BACKWARD_POST once it ends."""
+    events = []
+    _prefetch_order_worker(0, 1, mode, events)
+    i_pre = events.index(("prefetch", 1))
+    i_post = events.index(("post", 2))
+    assert (i_pre < i_post) if mode == "BACKWARD_PRE" else (i_pre > i_post), events
