@@ -92,6 +92,10 @@ class ParallelConfig:
     on a single node it is FULL_SHARD).
     ``cpu_offload`` is accepted for YAML compatibility; the engine keeps all
     state in HBM (it is never read by the reference either).
+    ``param_dtype`` is the compute and gathered-parameter dtype.  Gradients
+    are always accumulated and reduced in float32 and the RoPE tables are
+    float32 whatever ``reduce_dtype`` / ``buffer_dtype`` say (a warning is
+    issued when ``reduce_dtype`` asks for less).
     """
 
     tp_size: int = 1

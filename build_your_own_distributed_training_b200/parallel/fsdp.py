@@ -42,6 +42,7 @@ package's NVLink peer-memory kernels).
 from __future__ import annotations
 
 import contextlib
+import warnings
 from dataclasses import dataclass, field
 from typing import Any, Iterable
 
@@ -521,6 +522,10 @@ def wrap_model_with_fsdp(model: nn.Module, ctx: Any, cfg: ParallelConfig,
     if cfg.backward_prefetch not in VALID_PREFETCH:
         raise ValueError(f"Unknown backward_prefetch={cfg.backward_prefetch!r}; valid: "
                          f"{sorted(VALID_PREFETCH)}.")
+    policy = build_mixed_precision(cfg)
+    if policy.reduce_dtype != torch.float32:
+        warnings.warn(f"reduce_dtype={cfg.reduce_dtype!r}: this engine accumulates and reduces gradients in "
+                      "float32 regardless (more precise than the requested dtype).", stacklevel=2)
     return FullyShardedModel(model, ctx, cfg, transformer_layer_cls, comm=comm)
 
 
