@@ -334,6 +334,37 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ x, long ld, const float*
   }
 }
 
+// Same rotation, eight consecutive pairs per thread with 16-byte accesses
+// (half-head a multiple of 8 and rows 16-byte aligned; the host checks).
+__global__ void rope_vec8_kernel(__nv_bfloat16* __restrict__ x, long ld, const float* __restrict__ cos_t,
+                                 const float* __restrict__ sin_t, int M, int rope_cols, int hd, int seqlen,
+                                 float sign) {
+  const int half = hd >> 1;
+  const int groups = rope_cols / 16;  // 8-pair groups per row
+  const long total = (long)M * groups;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long row = i / groups;
+    const int p = (int)(i % groups) * 8;
+    const int head = p / half, j = p % half;
+    const int pos = (int)(row % seqlen);
+    __nv_bfloat16* b = x + row * ld + head * hd;
+    uint4 q1 = *reinterpret_cast<const uint4*>(b + j), q2 = *reinterpret_cast<const uint4*>(b + j + half);
+    float c[8], sn[8];
+    load_w8(cos_t + (long)pos * hd, j, c);
+    load_w8(sin_t + (long)pos * hd, j, sn);
+    uint32_t *u1 = &q1.x, *u2 = &q2.x;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 a = unpack_bf16x2(u1[k]), bb = unpack_bf16x2(u2[k]);
+      const float s0 = sign * sn[2 * k], s1 = sign * sn[2 * k + 1];
+      u1[k] = pack_bf16x2(a.x * c[2 * k] - bb.x * s0, a.y * c[2 * k + 1] - bb.y * s1);
+      u2[k] = pack_bf16x2(bb.x * c[2 * k] + a.x * s0, bb.y * c[2 * k + 1] + a.y * s1);
+    }
+    *reinterpret_cast<uint4*>(b + j) = q1;
+    *reinterpret_cast<uint4*>(b + j + half) = q2;
+  }
+}
+
 // ---------------------------------------------------------------- SwiGLU bwd
 __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ da, const __nv_bfloat16* __restrict__ gu,
                                   __nv_bfloat16* __restrict__ dgu, int M, int F) {
@@ -355,6 +386,40 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ da, const __
     }
     *reinterpret_cast<uint32_t*>(dgu + row * 2L * F + c) = pack_bf16x2(dg[0], dg[1]);
     *reinterpret_cast<uint32_t*>(dgu + row * 2L * F + F + c) = pack_bf16x2(du[0], du[1]);
+  }
+}
+
+// Same arithmetic, eight elements per thread with 16-byte accesses (F % 8 == 0).
+__global__ void swiglu_bwd_vec8_kernel(const __nv_bfloat16* __restrict__ da, const __nv_bfloat16* __restrict__ gu,
+                                       __nv_bfloat16* __restrict__ dgu, int M, int F) {
+  const int groups = F / 8;
+  const long total = (long)M * groups;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long row = i / groups;
+    const int c = (int)(i % groups) * 8;
+    const uint4 qa = *reinterpret_cast<const uint4*>(da + row * F + c);
+    const uint4 qg = *reinterpret_cast<const uint4*>(gu + row * 2L * F + c);
+    const uint4 qu = *reinterpret_cast<const uint4*>(gu + row * 2L * F + F + c);
+    const uint32_t *ua = &qa.x, *ug = &qg.x, *uu = &qu.x;
+    uint4 og, ou;
+    uint32_t *pg = &og.x, *pu = &ou.x;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 a = unpack_bf16x2(ua[k]), g = unpack_bf16x2(ug[k]), u = unpack_bf16x2(uu[k]);
+      const float gg[2] = {g.x, g.y}, uv[2] = {u.x, u.y}, aa[2] = {a.x, a.y};
+      float dg[2], du[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float sg = 1.f / (1.f + expf(-gg[e]));
+        const float silu = gg[e] * sg;
+        dg[e] = aa[e] * uv[e] * sg * (1.f + gg[e] * (1.f - sg));
+        du[e] = aa[e] * silu;
+      }
+      pg[k] = pack_bf16x2(dg[0], dg[1]);
+      pu[k] = pack_bf16x2(du[0], du[1]);
+    }
+    *reinterpret_cast<uint4*>(dgu + row * 2L * F + c) = og;
+    *reinterpret_cast<uint4*>(dgu + row * 2L * F + F + c) = ou;
   }
 }
 
@@ -667,6 +732,17 @@ void rope_apply(torch::Tensor x, torch::Tensor cos_t, torch::Tensor sin_t, int64
   const int M = (int)x.size(0);
   const long total = (long)M * rope_cols / 2;
   if (total == 0) return;
+  const bool vec = (hd / 2) % 8 == 0 && rope_cols % hd == 0 && x.stride(0) % 8 == 0 &&
+                   (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(cos_t.data_ptr()) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(sin_t.data_ptr()) & 15) == 0;
+  if (vec) {
+    rope_vec8_kernel<<<grid_for(total / 8, 256), 256, 0, cur_stream()>>>(
+        reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), x.stride(0), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
+        M, (int)rope_cols, (int)hd, (int)seqlen, (float)sign);
+    DTB_LAUNCH_CHECK();
+    return;
+  }
   rope_kernel<<<grid_for(total, 256), 256, 0, cur_stream()>>>(
       reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), x.stride(0), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), M,
       (int)rope_cols, (int)hd, (int)seqlen, (float)sign);
@@ -686,6 +762,14 @@ void swiglu_bwd(torch::Tensor da, torch::Tensor gu, torch::Tensor dgu) {
   TORCH_CHECK(F % 2 == 0 && gu.size(1) == 2 * F && da.is_contiguous() && gu.is_contiguous(), "swiglu_bwd shapes");
   const long total = (long)M * F / 2;
   if (total == 0) return;
+  if (F % 8 == 0 && (reinterpret_cast<uintptr_t>(da.data_ptr()) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(gu.data_ptr()) & 15) == 0 && (reinterpret_cast<uintptr_t>(dgu.data_ptr()) & 15) == 0) {
+    swiglu_bwd_vec8_kernel<<<grid_for(total / 4, 256), 256, 0, cur_stream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(da.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()),
+        reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()), M, F);
+    DTB_LAUNCH_CHECK();
+    return;
+  }
   swiglu_bwd_kernel<<<grid_for(total, 256), 256, 0, cur_stream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(da.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()), M, F);

@@ -177,14 +177,17 @@ def test_rmsnorm_backward_is_deterministic():
     del _RMSNormFn
 
 
-def test_rope_bwd_is_transpose():
+@pytest.mark.parametrize("pad", [0, 4])
+def test_rope_bwd_is_transpose(pad):
+    """pad=0: 16-byte vector kernel; pad=4 (rows not 16-byte aligned): the scalar kernel."""
     from build_your_own_distributed_training_b200.ops.rope import precompute_rope_cache, rope_backward_, rope_forward
     hd, seqlen = 128, 128
     cos, sin = precompute_rope_cache(hd, 256, 10000.0, DEV)
-    d = _rand(2 * seqlen, 6 * hd)
+    base = _rand(2 * seqlen, 6 * hd + pad)
+    d = base[:, :6 * hd]
     ref = d.float().cpu().clone()
     rope_backward_(ref, cos.cpu(), sin.cpu(), 4 * hd, hd, seqlen)
-    out = d.clone()
+    out = base.clone()[:, :6 * hd]  # keeps the padded row stride
     rope_backward_(out, cos, sin, 4 * hd, hd, seqlen)
     assert _rel(out.cpu(), ref) < 1e-2
     # forward then backward is the identity (rotation is orthogonal)
@@ -194,9 +197,11 @@ def test_rope_bwd_is_transpose():
     assert _rel(y, d.float().cpu()) < 1e-5
 
 
-def test_swiglu_bwd():
+@pytest.mark.parametrize("Fh", [256, 100])
+def test_swiglu_bwd(Fh):
+    """Fh % 8 == 0: 16-byte vector kernel; Fh = 100: the two-element kernel."""
     from build_your_own_distributed_training_b200.ops.linear import swiglu_backward
-    M, Fh = 300, 256
+    M = 300
     gu, da = _rand(M, 2 * Fh), _rand(M, Fh)
     out = swiglu_backward(da, gu, Fh)
     ref = swiglu_backward(da.cpu().float(), gu.cpu().float(), Fh)
