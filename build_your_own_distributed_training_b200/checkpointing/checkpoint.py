@@ -104,6 +104,15 @@ def load_checkpoint(model: Any, optimizer: torch.optim.Optimizer, scheduler: Any
         meta = json.load(f)
     if full is None:
         full = meta.get("format") == "full"
+    if not full:
+        saved = (meta.get("world_size"), meta.get("tp_size"), meta.get("dp_size"))
+        now = (ctx.world_size, ctx.dims.tp_size, ctx.dims.dp_size)
+        if saved != now:
+            raise ValueError(
+                f"[rank {ctx.rank}] sharded checkpoint {path} was written by world_size={saved[0]} "
+                f"(tp={saved[1]}, dp={saved[2]}) but this run is world_size={now[0]} (tp={now[1]}, "
+                f"dp={now[2]}): shards are only valid on the topology that wrote them; resume with "
+                "that topology or save/load the full format.")
     rank_dir = os.path.join(path, f"rank_{ctx.rank}")
     if full:
         load_model_state_dict(model, safe_load(os.path.join(path, "model_full.pt")), full=True)

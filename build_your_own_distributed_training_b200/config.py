@@ -5,8 +5,7 @@ drive ``train.py`` here (reference: ``src/config.py:44-215`` for the sections,
 ``src/config.py:219-326`` for the top level).  Two additions:
 
 * ``kernels:`` — an optional section holding switches for the native fast
-  paths (fused collectives, CUDA-graph capture of the step).  Files without it
-  parse unchanged.
+  paths (fused collectives).  Files without it parse unchanged.
 * ``data.dataset_path: uniform`` — uniform-random token ids, the synthetic
   workload used by the throughput benchmarks.
 

@@ -172,7 +172,7 @@ static PeerPtrs make_peers(const std::vector<int64_t>& bases) {
 
 static int blocks_for(long work_items, int nt) {
   long b = (work_items + nt - 1) / nt;
-  return (int)std::max<long>(1, std::min<long>(b, 148L * 8));
+  return (int)std::max<long>(1, std::min<long>(b, 8L * device_sm_count()));
 }
 
 }  // namespace comm

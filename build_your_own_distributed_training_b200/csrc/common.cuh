@@ -13,6 +13,20 @@
 
 namespace dtb {
 
+// Streaming-multiprocessor count of the current device (148 on a B200), queried
+// once per device and cached; grids are sized as multiples of it.
+inline int device_sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
 // error codes written to the device error word
 enum : int {
   ERR_NONE = 0,

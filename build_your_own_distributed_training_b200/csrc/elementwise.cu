@@ -607,7 +607,7 @@ __global__ void __launch_bounds__(NT) sum_parts_kernel(const float* __restrict__
 
 static int grid_for(long n, int nt) {
   long g = (n + nt - 1) / nt;
-  return (int)std::max<long>(1, std::min<long>(g, 148L * 16));
+  return (int)std::max<long>(1, std::min<long>(g, 16L * device_sm_count()));
 }
 
 }  // namespace dtb
@@ -703,12 +703,15 @@ void rmsnorm_bwd_launch(const __nv_bfloat16* dy, const __nv_bfloat16* x, const v
 
 int rmsnorm_bwd_rows_per_cta(int M) {
   // enough CTAs to fill the GPU, few enough partial rows to keep the reduce cheap
-  return std::max(1, M / (148 * 4));
+  return std::max(1, M / (device_sm_count() * 4));
 }
 
 torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw_acc) {
   TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && dy.sizes() == x.sizes(), "rmsnorm_bwd: shapes");
   TORCH_CHECK(dw_acc.scalar_type() == at::kFloat && dw_acc.is_contiguous(), "rmsnorm_bwd: fp32 dw accumulator");
+  TORCH_CHECK(((reinterpret_cast<uintptr_t>(dy.data_ptr()) | reinterpret_cast<uintptr_t>(x.data_ptr()) |
+                reinterpret_cast<uintptr_t>(w.data_ptr())) & 15) == 0,
+              "rmsnorm_bwd: dy, x and w must start on 16-byte boundaries");
   const c10::cuda::CUDAGuard g(x.device());
   const int M = (int)x.size(0), D = (int)x.size(1);
   TORCH_CHECK(D * 4 <= 48 * 1024, "rmsnorm_bwd: D up to 12288");
@@ -856,7 +859,7 @@ torch::Tensor sumsq(torch::Tensor x) {
   TORCH_CHECK(x.scalar_type() == at::kFloat && x.is_contiguous(), "sumsq: contiguous fp32");
   const c10::cuda::CUDAGuard g(x.device());
   const long n = x.numel();
-  const int nb = 148 * 8;
+  const int nb = device_sm_count() * 8;
   auto part = torch::empty({nb}, x.options());
   auto out = torch::empty({}, x.options());
   auto st = cur_stream();

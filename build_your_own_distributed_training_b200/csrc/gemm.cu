@@ -644,15 +644,7 @@ static CUtensorMap make_map(const void* base, long inner, long rows, long row_st
   return m;
 }
 
-static int num_sms() {
-  static int n = 0;
-  if (!n) {
-    int dev;
-    DTB_CUDA(cudaGetDevice(&dev));
-    DTB_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
-  }
-  return n;
-}
+static int num_sms() { return device_sm_count(); }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool PAIR>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t st) {

@@ -3,6 +3,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <cstdint>
 #include <mutex>
 
 #include "noalloc.h"
@@ -44,6 +45,9 @@ extern "C" int dtb_rmsnorm_bwd_noalloc(const void* dy, const void* x, const void
                                        void* stream) {
   if (!dy || !x || !w || !rstd || !dx || !dw_acc || rows <= 0 || dim <= 0 || dim % 8 != 0)
     return DTB_NOALLOC_BAD_ARGUMENT;
+  // the kernels move dy, x, dx and w in 16-byte vectors
+  const auto misaligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; };
+  if (misaligned(dy) || misaligned(x) || misaligned(dx) || misaligned(w)) return DTB_NOALLOC_BAD_ARGUMENT;
   if (dim > DTB_NOALLOC_MAX_DIM) return DTB_NOALLOC_TOO_LARGE;
   // as many CTAs as both the scratch array and kMaxCtas allow
   const long max_ctas = DTB_NOALLOC_SCRATCH_FLOATS / dim < kMaxCtas ? DTB_NOALLOC_SCRATCH_FLOATS / dim : kMaxCtas;
@@ -53,7 +57,9 @@ extern "C" int dtb_rmsnorm_bwd_noalloc(const void* dy, const void* x, const void
   float* part = nullptr;
   const int rc = scratch_for_current_device(&part);
   if (rc != DTB_NOALLOC_OK) return rc;
-  cudaGetLastError();  // clear a stale launch error so the check below sees ours
+  // An error left pending by the caller's own earlier work is reported and left
+  // in place for the caller, not consumed here.
+  if (cudaPeekAtLastError() != cudaSuccess) return DTB_NOALLOC_CUDA_ERROR;
   rmsnorm_bwd_launch(static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x), w,
                      w_is_fp32 != 0, rstd, static_cast<__nv_bfloat16*>(dx), dw_acc, part, rows, dim, rows_per_cta,
                      static_cast<cudaStream_t>(stream));
@@ -63,9 +69,9 @@ extern "C" int dtb_rmsnorm_bwd_noalloc(const void* dy, const void* x, const void
 extern "C" const char* dtb_noalloc_error_string(int code) {
   switch (code) {
     case DTB_NOALLOC_OK: return "ok";
-    case DTB_NOALLOC_BAD_ARGUMENT: return "bad argument: null pointer, rows < 1, or dim not a positive multiple of 8";
+    case DTB_NOALLOC_BAD_ARGUMENT: return "bad argument: null pointer, a dy/x/dx/w pointer not 16-byte aligned, rows < 1, or dim not a positive multiple of 8";
     case DTB_NOALLOC_TOO_LARGE: return "dim above DTB_NOALLOC_MAX_DIM (12288): the fixed scratch/shared-memory limit";
-    case DTB_NOALLOC_CUDA_ERROR: return "CUDA error (scratch address lookup or kernel launch failed)";
+    case DTB_NOALLOC_CUDA_ERROR: return "CUDA error (an error already pending on entry, scratch address lookup or kernel launch failed)";
     default: return "unknown code";
   }
 }

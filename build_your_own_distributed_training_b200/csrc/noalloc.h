@@ -39,7 +39,9 @@ extern "C" {
 // dy, x, dx: bf16 [rows, dim] row-major; w: [dim] bf16 (w_is_fp32 = 0) or fp32;
 // rstd: fp32 [rows] saved by the forward; dw_acc: fp32 [dim], the weight
 // gradient is ADDED to it.  Runs on `stream` (a cudaStream_t, may be 0).
-// Returns one of the DTB_NOALLOC_* codes; allocates nothing.
+// Returns one of the DTB_NOALLOC_* codes; allocates nothing.  If a CUDA error
+// is already pending on entry (cudaPeekAtLastError), nothing is launched, the
+// call returns DTB_NOALLOC_CUDA_ERROR and the error stays pending.
 int dtb_rmsnorm_bwd_noalloc(const void* dy, const void* x, const void* w, int w_is_fp32, const float* rstd,
                             void* dx, float* dw_acc, int rows, int dim, void* stream);
 

@@ -3,14 +3,15 @@
 ``build_profiler`` / ``communication_fraction`` / ``text_summary`` /
 ``export_chrome_trace`` behave as ``src/observability/profiler.py:35-141``.
 The collective-name hints also match this package's own peer-memory kernels
-(``peer_`` prefix), and ``fused_kernel_share`` reports fused
-GEMM+collective kernels separately, since their time cannot be split into
-"compute" and "communication" by name.
+(``peer_`` prefix), and ``CommComputeBreakdown.fused_cuda_us`` reports fused
+GEMM+collective kernels separately (``is_fused_comm_kernel``), since their time
+cannot be split into "compute" and "communication" by name.
 """
 
 from __future__ import annotations
 
 import os
+import re
 from dataclasses import dataclass
 
 import torch
@@ -18,7 +19,28 @@ from torch.profiler import ProfilerActivity, profile, schedule, tensorboard_trac
 
 COMM_HINTS = ("nccl", "all_reduce", "allreduce", "all_gather", "allgather", "reduce_scatter",
               "reducescatter", "broadcast", "c10d", "peer_", "dev_barrier")
-FUSED_HINTS = ("gemm_ar", "gemm_rs", "ag_gemm")
+# Kernels that do a GEMM and a collective in one launch.  The tcgen05 GEMM is one
+# template, ``gemm_tcgen05_kernel<BN, STAGES, A_MN, B_MN, EPI, PAIR>``; its peer
+# epilogue (EPI == 6, csrc/gemm.cu ``EPI_PEER_AR``) sums the TP group's tiles
+# over NVLink (all-reduce, or reduce-scatter under sequence parallelism).
+FUSED_HINTS = ("ag_gemm", "gemm_ar", "gemm_rs")
+PEER_EPILOGUE_ID = 6
+_GEMM_TEMPLATE = re.compile(r"gemm_tcgen05_kernel<\s*(\d+)\s*,\s*(\d+)\s*,\s*(\d+)\s*,\s*(\d+)\s*,\s*(\d+)")
+
+
+def is_fused_comm_kernel(name: str) -> bool:
+    """True for a kernel that fuses a collective into its GEMM (by template epilogue id or name)."""
+    m = _GEMM_TEMPLATE.search(name)
+    if m is not None:
+        return int(m.group(5)) == PEER_EPILOGUE_ID
+    low = name.lower()
+    return any(h in low for h in FUSED_HINTS)
+
+
+def is_comm_kernel(name: str) -> bool:
+    """True for a pure communication kernel (NCCL, c10d, this package's peer copies)."""
+    low = name.lower()
+    return not is_fused_comm_kernel(name) and any(h in low for h in COMM_HINTS)
 
 
 @dataclass
@@ -58,10 +80,9 @@ def communication_fraction(prof: profile) -> CommComputeBreakdown:
     for evt in prof.key_averages():
         us = float(getattr(evt, "self_device_time_total", getattr(evt, "self_cuda_time_total", 0.0)))
         total += us
-        name = evt.key.lower()
-        if any(h in name for h in FUSED_HINTS):
+        if is_fused_comm_kernel(evt.key):
             fused += us
-        elif any(h in name for h in COMM_HINTS):
+        elif is_comm_kernel(evt.key):
             comm += us
     return CommComputeBreakdown(total, comm, total - comm - fused,
                                 comm / total if total > 0 else 0.0, fused)

@@ -5,12 +5,15 @@ Keys are the model's parameter FQNs (``tok_embeddings.weight``,
 saved under both names), as with the reference's FSDP state dicts
 (``src/parallelism/fsdp_utils.py:230-378``).
 
-Sharded form (one dict per rank): every parameter is split into even dim-0
-chunks over the shard (dp) group, on top of its tensor-parallel split, and
-this rank stores its chunk as a plain fp32 tensor.  A ``__layout__`` entry
+Sharded form (one dict per rank): each rank writes exactly the fp32 values
+it owns, with no communication.  The engine shards a block's flat buffer into
+contiguous ranges, so a rank's piece of a parameter is a contiguous range of
+that parameter's flattened (TP-local) values; it is stored as a 1-D fp32
+tensor (empty where the rank owns none of it).  A ``__layout__`` entry
 records, per key, the TP split (``row``/``col``/``rep``), the TP-local shape
-and the chunk's row range, which is what the reference's DTensor values
-encoded.  Optimizer state uses the same keys:
+and the flat range ``[lo, hi)``, which is what the reference's DTensor values
+encoded.  Loading reads the same ranges back, so a sharded checkpoint resumes
+on the topology that wrote it (the loader checks ``meta.json`` first).  Optimizer state uses the same keys:
 ``{"state": {fqn: {"step", "exp_avg", "exp_avg_sq"}}, "param_groups": [...]}``.
 Everything is tensors, ints, floats and strings, so the files load with
 ``torch.load(weights_only=True)``.
@@ -28,12 +31,6 @@ import torch.distributed as dist
 import torch.nn as nn
 
 from .fsdp import FlatUnit, FullyShardedModel
-
-
-def _chunk_rows(rows: int, world: int, rank: int) -> tuple[int, int]:
-    per = -(-rows // world) if rows else 0
-    lo = min(rows, rank * per)
-    return lo, min(rows, lo + per)
 
 
 def _aliases(model: FullyShardedModel) -> dict[int, list[str]]:
@@ -63,31 +60,43 @@ def _tp_gather(t: torch.Tensor, kind: str, model: FullyShardedModel) -> torch.Te
     return torch.cat(parts, dim=0 if kind == "row" else 1)
 
 
+def _local_piece(u: FlatUnit, e: Any, rank: int) -> tuple[int, int, int]:
+    """(lo, hi, shard_offset): the range [lo, hi) of entry ``e``'s flattened values that
+    lies in ``rank``'s shard of unit ``u``, and where it starts inside that shard."""
+    s_lo, s_hi = u.shard_range(rank)
+    a, b = max(e.offset, s_lo), min(e.offset + e.numel, s_hi)
+    if b <= a:
+        return 0, 0, 0
+    return a - e.offset, b - e.offset, a - s_lo
+
+
 def _unit_entries(model: FullyShardedModel, flat_shards: dict[str, list[torch.Tensor]], *, full: bool
                   ) -> tuple[dict[str, dict[str, torch.Tensor]], dict[str, Any]]:
     aliases = _aliases(model)
     out: dict[str, dict[str, torch.Tensor]] = {k: {} for k in flat_shards}
     layout: dict[str, Any] = {}
     W, R = model.shard_world, model.shard_rank
+    tpr = model.ctx.dims.tp_rank if model.ctx else 0
     for ui, u in enumerate(model.units):
-        fulls = {k: _flat_full(model, u, v[ui]) for k, v in flat_shards.items()}
+        if full:
+            fulls = {k: _flat_full(model, u, v[ui]) for k, v in flat_shards.items()}
         for e in u.entries:
             names = aliases.get(id(e.param), [e.fqn])
-            for k, flat in fulls.items():
-                local = flat[e.offset:e.offset + e.numel].view(e.shape)
-                if full:
+            if full:
+                for k, flat in fulls.items():
+                    local = flat[e.offset:e.offset + e.numel].view(e.shape)
                     val = _tp_gather(local, e.tp_kind, model).detach().cpu().clone()
-                else:
-                    lo, hi = _chunk_rows(e.shape[0], W, R)
-                    val = local[lo:hi].detach().cpu().clone()
+                    for n in names:
+                        out[k][n] = val
+                continue
+            lo, hi, so = _local_piece(u, e, R)
+            for k, shards in flat_shards.items():
+                val = shards[ui].detach()[so:so + (hi - lo)].float().cpu().clone()
                 for n in names:
                     out[k][n] = val
-            if not full:
-                lo, hi = _chunk_rows(e.shape[0], W, R)
-                for n in names:
-                    layout[n] = {"tp": e.tp_kind, "local_shape": list(e.shape), "rows": [lo, hi],
-                                 "dp_world": W, "dp_rank": R, "tp_size": model.tp_size,
-                                 "tp_rank": model.ctx.dims.tp_rank if model.ctx else 0}
+            for n in names:
+                layout[n] = {"tp": e.tp_kind, "local_shape": list(e.shape), "flat": [lo, hi],
+                             "dp_world": W, "dp_rank": R, "tp_size": model.tp_size, "tp_rank": tpr}
     return out, layout
 
 
@@ -105,17 +114,20 @@ def get_model_state_dict(model: nn.Module, *, full: bool) -> dict[str, Any]:
 
 def _scatter_into_units(model: FullyShardedModel, values: dict[str, torch.Tensor], *, full: bool,
                         targets: list[torch.Tensor]) -> None:
-    """Write per-FQN values (chunks or full tensors) back into per-unit flat shards."""
-    W, R = model.shard_world, model.shard_rank
+    """Write per-FQN values back into per-unit flat shards: complete tensors (full form, any
+    topology, each rank keeps its TP slice and flat range) or this rank's own flat ranges
+    (sharded form, no communication)."""
+    R = model.shard_rank
     tpr = model.ctx.dims.tp_rank if model.ctx else 0
     for ui, u in enumerate(model.units):
         dev = targets[ui].device
-        flat = torch.zeros(u.numel, dtype=torch.float32, device=dev)
+        s_lo, s_hi = u.shard_range(R)
+        shard = torch.zeros(s_hi - s_lo, dtype=torch.float32, device=dev)
         for e in u.entries:
             if e.fqn not in values:
                 raise KeyError(f"state dict is missing {e.fqn!r}")
-            v = values[e.fqn].to(dev, torch.float32)
-            seg = flat[e.offset:e.offset + e.numel].view(e.shape)
+            lo, hi, so = _local_piece(u, e, R)
+            v = values[e.fqn]
             if full:
                 if e.tp_kind == "row":
                     n = e.shape[0]
@@ -125,17 +137,12 @@ def _scatter_into_units(model: FullyShardedModel, values: dict[str, torch.Tensor
                     v = v[:, tpr * n:(tpr + 1) * n]
                 if tuple(v.shape) != tuple(e.shape):
                     raise ValueError(f"{e.fqn}: shape {tuple(v.shape)} != expected {tuple(e.shape)}")
-                seg.copy_(v)
-            else:
-                lo, hi = _chunk_rows(e.shape[0], W, R)
-                if v.shape[0] != hi - lo:
-                    raise ValueError(f"{e.fqn}: chunk has {v.shape[0]} rows, expected {hi - lo}; the "
-                                     "checkpoint was saved with another topology")
-                seg[lo:hi].copy_(v)
-        if not full and W > 1:
-            dist.all_reduce(flat, group=model.comm.group)
-        lo, hi = u.shard_range(R)
-        targets[ui].copy_(flat[lo:hi].to(targets[ui].dtype))
+                v = v.reshape(-1)[lo:hi]
+            elif v.dim() != 1 or v.numel() != hi - lo:
+                raise ValueError(f"{e.fqn}: shard holds {v.numel()} values, this rank owns {hi - lo}; the "
+                                 "checkpoint was saved with another topology")
+            shard[so:so + (hi - lo)].copy_(v.to(dev, torch.float32))
+        targets[ui].copy_(shard.to(targets[ui].dtype))
 
 
 def load_model_state_dict(model: nn.Module, state_dict: dict[str, Any], *, full: bool) -> None:

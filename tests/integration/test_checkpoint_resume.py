@@ -43,3 +43,27 @@ def _run(rank, world, tp, tmp, full):
 @pytest.mark.parametrize("world,tp,full", [(1, 1, False), (2, 1, False), (4, 2, False), (4, 2, True)])
 def test_resume_is_bit_exact(tmp_path, world, tp, full):
     run_distributed(_run, world, tp, str(tmp_path), full)
+
+
+def _save_at(rank, world, tp, tmp):
+    ctx = build_process_context(tp, backend="gloo", verbose=False)
+    cfg = tiny_config(tmp, parallel__tp_size=tp, run_id="topo")
+    t = Trainer(cfg, ctx=ctx, gpu_type="cpu")
+    w, _ = t._next_window()
+    train_step(t.model, w, t.optimizer, t.scheduler, ctx, cfg, gpu_type="cpu")
+    save_checkpoint(t.model, t.optimizer, t.scheduler, 1, cfg, ctx, full=False)
+
+
+def _load_at(rank, world, tp, tmp):
+    import glob
+    ctx = build_process_context(tp, backend="gloo", verbose=False)
+    cfg = tiny_config(tmp, parallel__tp_size=tp, run_id="topo")
+    t = Trainer(cfg, ctx=ctx, gpu_type="cpu")
+    path = sorted(glob.glob(f"{tmp}/**/step_1", recursive=True))[0]
+    with pytest.raises(ValueError, match="topology that wrote them"):
+        load_checkpoint(t.model, t.optimizer, t.scheduler, path, ctx)
+
+
+def test_sharded_load_on_another_topology_fails_early(tmp_path):
+    run_distributed(_save_at, 2, 1, str(tmp_path))   # tp1 x dp2
+    run_distributed(_load_at, 2, 2, str(tmp_path))   # tp2 x dp1: same world size, other layout

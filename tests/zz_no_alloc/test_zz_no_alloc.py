@@ -76,3 +76,16 @@ def test_noalloc_rejects_sizes_beyond_the_limit():
     assert rc == 2 and b"12288" in err(rc)
     rc = fn(t.data_ptr(), t.data_ptr(), acc.data_ptr(), 1, r.data_ptr(), t.data_ptr(), acc.data_ptr(), 8, 100, None)
     assert rc == 1
+
+
+def test_noalloc_rejects_misaligned_pointers_without_launching():
+    fn, err = _entry()
+    t = torch.zeros(8 * 64 + 8, device=DEV, dtype=torch.bfloat16)
+    x = t[1:1 + 8 * 64]  # 2 bytes past a 16-byte boundary
+    r = torch.ones(8, device=DEV)
+    acc = torch.zeros(64, device=DEV)
+    w = torch.ones(64, device=DEV)
+    rc = fn(x.data_ptr(), x.data_ptr(), w.data_ptr(), 1, r.data_ptr(), x.data_ptr(), acc.data_ptr(), 8, 64, None)
+    assert rc == 1 and b"16-byte" in err(rc)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(acc) == 0  # nothing ran
