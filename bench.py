@@ -165,16 +165,52 @@ def timed_loop(step_fn, steps: int, world: int) -> tuple[float, float]:
     return float(dev[0]), float(dev[1])
 
 
-def count_launches(step_fn, prefixes: tuple[str, ...]) -> int:
+KERNEL_CLASSES = (
+    # (class, substrings) in match order; the first match wins
+    ("gemm+collective", ()),  # tcgen05 GEMM with the peer epilogue, see observability.profiler
+    ("gemm", ("gemm_tcgen05", "gemm", "cutlass", "nvjet", "sm100_xmma")),
+    ("attention", ("attn_", "flash", "fmha", "sdpa", "cudnn")),
+    ("optimizer", ("adamw", "sumsq", "sum_parts", "multi_tensor", "foreach")),
+    ("collective", ("nccl", "peer_", "dev_barrier")),
+    ("norm/rope/swiglu/ce/embedding", ("rmsnorm", "rope_", "swiglu", "ce_", "count_valid", "embedding",
+                                       "reduce_partials")),
+)
+
+
+def profile_one_step(step_fn, prefixes: tuple[str, ...]) -> tuple[int, dict]:
+    """Runs one extra (untimed) step under torch.profiler; returns the number of this
+    package's kernel launches in it and the summed device time per kernel class (ms).
+    Kernels on different streams overlap, so the classes can add up to more than the
+    step's device time; ``step_ms`` is the step's own CUDA-event time."""
     from torch.profiler import ProfilerActivity, profile
+    sys.path.insert(0, HERE)
+    from build_your_own_distributed_training_b200.observability.profiler import is_fused_comm_kernel
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        e0.record()
         step_fn()
+        e1.record()
         torch.cuda.synchronize()
     n = 0
+    split: dict[str, float] = {}
     for e in prof.events():
-        if e.device_type == torch.autograd.DeviceType.CUDA and any(p in e.name for p in prefixes):
+        if e.device_type != torch.autograd.DeviceType.CUDA:
+            continue
+        if any(p in e.name for p in prefixes):
             n += 1
-    return n
+        low = e.name.lower()
+        cls = "other"
+        if is_fused_comm_kernel(e.name):
+            cls = "gemm+collective"
+        else:
+            for name, keys in KERNEL_CLASSES[1:]:
+                if any(k in low for k in keys):
+                    cls = name
+                    break
+        split[cls] = split.get(cls, 0.0) + e.time_range.elapsed_us() / 1e3
+    split = {k: round(v, 2) for k, v in sorted(split.items(), key=lambda kv: -kv[1])}
+    split["step_ms"] = round(e0.elapsed_time(e1), 2)
+    return n, split
 
 
 # ----------------------------------------------------------------------------- native
@@ -215,7 +251,7 @@ def run_native(args, n: int, rank: int, world: int) -> dict:
         step()
     with ClockSampler(rank == 0) as clk:
         dev_s, host_s = timed_loop(step, args.steps, world)
-    launches = count_launches(step, ("gemm_tcgen05", "attn_", "rmsnorm_", "rope_", "swiglu_", "embedding_",
+    launches, split = profile_one_step(step, ("gemm_tcgen05", "attn_", "rmsnorm_", "rope_", "swiglu_", "embedding_",
                                      "ce_", "count_valid", "adamw", "sumsq", "sum_parts",
                                      "reduce_partials", "peer_", "dev_barrier"))
     from build_your_own_distributed_training_b200.ops._ext import native
@@ -223,7 +259,7 @@ def run_native(args, n: int, rank: int, world: int) -> dict:
     if err:
         raise RuntimeError(f"device error word set: {err}")
     return dict(tp=tp, dp=dp, mb=mb, dev_s=dev_s, host_s=host_s, clocks=clk.summary(n),
-                launches_per_step=launches,
+                launches_per_step=launches, split=split,
                 h2d=2 * mb * SEQ * 8, d2h=16,
                 peak_mem=torch.cuda.max_memory_allocated())
 
@@ -355,6 +391,8 @@ def main() -> None:
         "gpu_launches": res["launches_per_step"] * args.steps,
         "peak_mem_gb": round(res["peak_mem"] / 1e9, 1),
     }
+    if res.get("split"):
+        out["device_ms_by_kernel_class"] = res["split"]
     if args.impl == "reference":
         out["impl"] = "reference"
         out["config"]["optimizer"] = res["ref_optimizer"]

@@ -39,6 +39,18 @@ void peer_all_reduce_bf16(std::vector<int64_t> bases, int64_t src_off, c10::opti
                           torch::Tensor out);
 void peer_reduce_rows_bf16(std::vector<int64_t> bases, int64_t src_off, int64_t row0, int64_t cols, torch::Tensor out);
 void wait_flag_probe(torch::Tensor flag, int64_t target, double timeout_s);
+int64_t gemm_ce_blocks(int64_t N);
+void gemm_ce_stats(torch::Tensor h, torch::Tensor w, torch::Tensor labels, torch::Tensor stats, torch::Tensor tgt,
+                   int64_t vocab_off, int64_t vocab_total, int64_t ignore);
+void gemm_ce_grad(torch::Tensor h, torch::Tensor w, torch::Tensor labels, torch::Tensor lse, torch::Tensor dloss,
+                  torch::Tensor inv_n, torch::Tensor out, int64_t vocab_off, int64_t vocab_total, int64_t ignore);
+void ce_stats_reduce(torch::Tensor stats, torch::Tensor tgt, torch::Tensor labels, int64_t vocab_off, int64_t v_local,
+                     int64_t vocab_total, int64_t ignore, torch::Tensor lse, torch::Tensor row_loss,
+                     c10::optional<torch::Tensor> xchg);
+void ce_peer_combine(std::vector<int64_t> bases, int64_t off, torch::Tensor labels, int64_t vocab_total, int64_t ignore,
+                     torch::Tensor lse, torch::Tensor row_loss);
+void ce_loss_finish(torch::Tensor row_loss, torch::Tensor labels, int64_t vocab_total, int64_t ignore,
+                    torch::Tensor loss, torch::Tensor inv_n);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels for B200-native 2-D parallel LLaMA training";
@@ -70,4 +82,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_all_reduce_bf16", &peer_all_reduce_bf16);
   m.def("peer_reduce_rows_bf16", &peer_reduce_rows_bf16);
   m.def("wait_flag_probe", &wait_flag_probe, "bounded wait on a flag (tests the timeout path)");
+  m.def("gemm_ce_blocks", &gemm_ce_blocks, "column blocks of the fused cross-entropy statistics");
+  m.def("gemm_ce_stats", &gemm_ce_stats, "head GEMM -> per-block log-sum-exp statistics and target logits");
+  m.def("gemm_ce_grad", &gemm_ce_grad, "head GEMM recomputed -> bf16 logit gradient");
+  m.def("ce_stats_reduce", &ce_stats_reduce);
+  m.def("ce_peer_combine", &ce_peer_combine, "vocabulary-parallel log-sum-exp over the TP group's heaps");
+  m.def("ce_loss_finish", &ce_loss_finish);
 }

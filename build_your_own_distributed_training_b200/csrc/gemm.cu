@@ -21,9 +21,12 @@
 //
 // Epilogues: bf16 / fp32 store (optional device-scalar alpha), fp32
 // accumulate into an existing buffer (weight gradients), residual add,
-// rotate-half RoPE on the q/k columns, and SwiGLU (B rows n and F+n of the
+// rotate-half RoPE on the q/k columns, SwiGLU (B rows n and F+n of the
 // stacked [W_gate; W_up] land in one 256-wide tile, the epilogue writes
-// silu(g)*u plus g and u for the backward).
+// silu(g)*u plus g and u for the backward), and the two halves of the fused
+// LM-head cross-entropy: per (row, column block) log-sum-exp statistics and
+// the target logit with no logits written (forward), and the logit gradient
+// (softmax - onehot) * coef recomputed from the accumulator (backward).
 //
 // No TMA multicast anywhere: each CTA loads its own tiles.
 #include <ATen/cuda/CUDAContext.h>
@@ -45,6 +48,9 @@ enum Epi : int {
   EPI_ROPE = 4,
   EPI_SWIGLU = 5,
   EPI_PEER_AR = 6,  // D = sum over the TP group of every rank's tile (+ R), through NVLink peer memory
+  EPI_CE_STATS = 7,     // per (row, column block): (max, sum exp(x - max)) -> ce_stats; x[label] -> ce_tgt
+  EPI_CE_GRAD = 8,      // D(bf16) = (exp(x - lse[row]) - [col == label]) * coef, coef = *alpha * *ce_inv_n
+  EPI_ACC_BF16OUT = 9,  // D(bf16) = acc + F[row, col], F an fp32 matrix (last step of a K-chunked GEMM)
 };
 
 constexpr int MAX_PEERS = 8;
@@ -72,6 +78,16 @@ struct GemmArgs {
   long stage_off, flag_off;
   uint32_t epoch;
   uint64_t timeout_ns;
+  // EPI_CE_STATS / EPI_CE_GRAD: labels of the rows, global vocabulary index of
+  // output column 0, vocabulary size, ignored label
+  const int64_t* labels;
+  long vocab_off, vocab_total, ignore;
+  float* ce_stats;        // [M, n_blocks] float2
+  float* ce_tgt;          // [M]
+  const float* ce_lse;    // [M]
+  const float* ce_inv_n;  // device scalar 1 / (number of valid labels)
+  const float* acc_in;    // EPI_ACC_BF16OUT: fp32 [M, N] with row stride ld_acc
+  long ld_acc;
 };
 
 constexpr int BM = 128;
@@ -193,6 +209,95 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
         store_bf16_32(gp, gr);
         store_bf16_32(up, ur);
         store_bf16_32(reinterpret_cast<__nv_bfloat16*>(a.D) + (long)row * a.ldd + c0 + c, h);
+      }
+    }
+    return;
+  }
+  constexpr float kLog2e = 1.4426950408889634f;
+  if (EPI == EPI_CE_STATS) {
+    // online log-sum-exp over this tile's columns of the row, base 2
+    const int n0 = nb * BN;
+    const long lab = row_ok ? a.labels[row] : a.ignore;
+    const long tc = (lab == a.ignore) ? -1 : lab - a.vocab_off - n0;  // target column inside this tile
+    float m = -INFINITY, s = 0.f, t = 0.f;
+    bool hit = false;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      if (n0 + c >= a.N) break;
+      float v[32];
+      tmem_ld32(trow + c, v);
+      const int nv = min(32, a.N - (n0 + c));
+      float cm = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < nv) cm = fmaxf(cm, v[i]);
+      if (tc >= c && tc < c + 32) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (tc == c + i) t = v[i];
+        hit = true;
+      }
+      const float mn = fmaxf(m, cm);
+      const float mb = mn * kLog2e;
+      float cs = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < nv) cs += ex2_approx(fmaf(v[i], kLog2e, -mb));
+      s = s * ex2_approx((m - mn) * kLog2e) + cs;
+      m = mn;
+    }
+    if (row_ok) {
+      reinterpret_cast<float2*>(a.ce_stats)[(long)row * a.n_blocks + nb] = make_float2(m, s);
+      if (hit) a.ce_tgt[row] = t;
+    }
+    return;
+  }
+  if (EPI == EPI_CE_GRAD) {
+    const int n0 = nb * BN;
+    const long lab = row_ok ? a.labels[row] : a.ignore;
+    const bool valid = row_ok && lab != a.ignore && lab >= 0 && lab < a.vocab_total;
+    const long tc = valid ? lab - a.vocab_off - n0 : -1;
+    const float coef = valid ? (*a.alpha) * (*a.ce_inv_n) : 0.f;
+    const float lse2 = row_ok ? a.ce_lse[row] * kLog2e : 0.f;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      if (n0 + c >= a.N) break;
+      float v[32];
+      tmem_ld32(trow + c, v);
+      if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          v[i] = (ex2_approx(fmaf(v[i], kLog2e, -lse2)) - (tc == c + i ? 1.f : 0.f)) * coef;
+        const int nv = min(32, a.N - (n0 + c));
+        __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(a.D) + (long)row * a.ldd + n0 + c;
+        if (nv >= 32) store_bf16_32(p, v);
+        else
+          for (int i = 0; i < nv; ++i) p[i] = __float2bfloat16_rn(v[i]);
+      }
+    }
+    return;
+  }
+  if (EPI == EPI_ACC_BF16OUT) {
+    const int n0 = nb * BN;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      if (n0 + c >= a.N) break;
+      float v[32];
+      tmem_ld32(trow + c, v);
+      if (row_ok) {
+        const int nv = min(32, a.N - (n0 + c));
+        const float* f = a.acc_in + (long)row * a.ld_acc + n0 + c;
+        __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(a.D) + (long)row * a.ldd + n0 + c;
+        if (nv >= 32) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            const float4 q = *reinterpret_cast<const float4*>(f + i);
+            v[i] += q.x; v[i + 1] += q.y; v[i + 2] += q.z; v[i + 3] += q.w;
+          }
+          store_bf16_32(p, v);
+        } else {
+          for (int i = 0; i < nv; ++i) p[i] = __float2bfloat16_rn(v[i] + f[i]);
+        }
       }
     }
     return;
@@ -699,6 +804,15 @@ static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, 
     case EPI_PEER_AR:
       if constexpr (!A_MN) { launch<BN, ST, A_MN, B_MN, EPI_PEER_AR, PAIR>(ta, tb, g, st); break; }
       TORCH_CHECK(false, "peer all-reduce epilogue needs a K-major A operand");
+    case EPI_CE_STATS:
+      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_CE_STATS, PAIR>(ta, tb, g, st); break; }
+      TORCH_CHECK(false, "cross-entropy epilogues need K-major operands");
+    case EPI_CE_GRAD:
+      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_CE_GRAD, PAIR>(ta, tb, g, st); break; }
+      TORCH_CHECK(false, "cross-entropy epilogues need K-major operands");
+    case EPI_ACC_BF16OUT:
+      if constexpr (!A_MN && B_MN) { launch<BN, ST, A_MN, B_MN, EPI_ACC_BF16OUT, PAIR>(ta, tb, g, st); break; }
+      TORCH_CHECK(false, "fp32-accumulator epilogue is built for the input-gradient layout (A K-major, B MN-major)");
     default: DTB_CHECK(false, "unknown epilogue %d", epi);
   }
 }
@@ -727,10 +841,21 @@ struct PeerCfg {
   int rs_row0 = 0, rs_rows = 0;  // reduce-scatter: this rank's output rows
 };
 
+// Fused LM-head cross-entropy epilogues (EPI_CE_STATS / EPI_CE_GRAD).
+struct CeCfg {
+  const int64_t* labels;
+  long vocab_off, vocab_total, ignore;
+  float* stats;
+  float* tgt;
+  const float* lse;
+  const float* inv_n;
+};
+
 static void gemm_impl(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_mn, bool b_mn, int64_t epi,
                       c10::optional<torch::Tensor> R, c10::optional<torch::Tensor> alpha,
                       c10::optional<torch::Tensor> cos_t, c10::optional<torch::Tensor> sin_t,
-                      c10::optional<torch::Tensor> D2, int64_t p0, int64_t p1, const PeerCfg* peer) {
+                      c10::optional<torch::Tensor> D2, int64_t p0, int64_t p1, const PeerCfg* peer,
+                      const CeCfg* ce = nullptr) {
   using namespace dtb;
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && D.is_cuda(), "gemm: CUDA tensors expected");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm: bf16 operands expected");
@@ -774,9 +899,30 @@ static void gemm_impl(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_
   int e = (int)epi;
   if (e == EPI_STORE_BF16 && f32out) e = EPI_STORE_F32;
   if (e == EPI_ACC_F32) TORCH_CHECK(f32out, "gemm: accumulate epilogue needs an fp32 output");
-  if (e == EPI_STORE_BF16 || e == EPI_RESIDUAL || e == EPI_ROPE || e == EPI_SWIGLU || e == EPI_PEER_AR)
+  if (e == EPI_STORE_BF16 || e == EPI_RESIDUAL || e == EPI_ROPE || e == EPI_SWIGLU || e == EPI_PEER_AR ||
+      e == EPI_CE_GRAD || e == EPI_ACC_BF16OUT)
     TORCH_CHECK(D.scalar_type() == at::kBFloat16, "gemm: bf16 output expected");
-  TORCH_CHECK(D.stride(1) == 1 && D.stride(0) % 8 == 0, "gemm: output rows must be contiguous and 16B aligned");
+  TORCH_CHECK((e == EPI_CE_STATS || e == EPI_CE_GRAD) == (ce != nullptr), "gemm: cross-entropy epilogue config");
+  if (ce != nullptr) {
+    g.labels = ce->labels;
+    g.vocab_off = ce->vocab_off;
+    g.vocab_total = ce->vocab_total;
+    g.ignore = ce->ignore;
+    g.ce_stats = ce->stats;
+    g.ce_tgt = ce->tgt;
+    g.ce_lse = ce->lse;
+    g.ce_inv_n = ce->inv_n;
+    if (e == EPI_CE_GRAD) TORCH_CHECK(alpha.has_value() && ce->lse && ce->inv_n, "gemm: ce grad needs alpha, lse, 1/n");
+  }
+  if (e == EPI_ACC_BF16OUT) {
+    TORCH_CHECK(R.has_value() && R->scalar_type() == at::kFloat && R->stride(1) == 1 && R->size(0) == M &&
+                    (reinterpret_cast<uintptr_t>(R->data_ptr()) & 15) == 0 && R->stride(0) % 4 == 0,
+                "gemm: fp32 accumulator input [M, N], rows 16-byte aligned");
+    g.acc_in = R->data_ptr<float>();
+    g.ld_acc = R->stride(0);
+  }
+  TORCH_CHECK(D.stride(1) == 1 && (D.stride(0) % 8 == 0 || e == EPI_CE_STATS),
+              "gemm: output rows must be contiguous and 16B aligned");
   if (alpha.has_value()) {
     TORCH_CHECK(alpha->scalar_type() == at::kFloat && alpha->is_cuda(), "gemm: alpha must be a CUDA fp32 scalar");
     g.alpha = alpha->data_ptr<float>();
@@ -820,8 +966,13 @@ static void gemm_impl(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_
   g.k_iters = (int)((K + BK - 1) / BK);
   g.num_tiles = g.m_blocks * g.n_blocks;
   g.flag_tiles = pair ? 2 * g.num_tiles : g.num_tiles;
-  TORCH_CHECK((g.rs_rows > 0 ? D.size(0) == g.rs_rows : D.size(0) == M) && D.size(1) == g.N,
-              "gemm: output shape mismatch");
+  if (e == EPI_CE_STATS) {
+    TORCH_CHECK(D.scalar_type() == at::kFloat && D.size(0) == M && D.size(1) == 2L * g.n_blocks,
+                "gemm: ce stats must be fp32 [M, 2 * n_blocks]");
+  } else {
+    TORCH_CHECK((g.rs_rows > 0 ? D.size(0) == g.rs_rows : D.size(0) == M) && D.size(1) == g.N,
+                "gemm: output shape mismatch");
+  }
   // tensor maps: A box = 128 rows (K-major) or 64 K-rows (MN-major); B likewise
   if (dtb_debug_enabled())
     fprintf(stderr, "[dtb] gemm M=%ld N=%d K=%ld a_mn=%d b_mn=%d epi=%d BN=%d A=%p B=%p D=%p alpha=%p\n", M, g.N, K,
@@ -874,4 +1025,48 @@ void gemm_peer_rs(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool b_mn, 
   PeerCfg pc{bases, (int)rank, (long)stage_off, (long)flag_off, (uint32_t)epoch, timeout_s, (int)row0, (int)rows};
   gemm_impl(A, B, D, false, b_mn, dtb::EPI_PEER_AR, R, c10::nullopt, c10::nullopt, c10::nullopt, c10::nullopt, 0, 0,
             &pc);
+}
+
+// Column blocks of the CE statistics for an N-column GEMM (same tile width rule as gemm_impl).
+int64_t gemm_ce_blocks(int64_t N) {
+  const int BN = N > 128 ? 256 : 128;
+  return (N + BN - 1) / BN;
+}
+
+static void dtb_ce_check_stats_shape(const torch::Tensor& stats, long M, long N) {
+  TORCH_CHECK(stats.scalar_type() == at::kFloat && stats.is_contiguous() && stats.dim() == 2 && stats.size(0) == M &&
+                  stats.size(1) == 2 * gemm_ce_blocks(N),
+              "ce: stats must be fp32 [M, 2 * gemm_ce_blocks(N)]");
+}
+
+// Fused LM-head cross-entropy, forward half: statistics of logits = h W^T
+// without writing the logits.  stats: fp32 [M, 2 * n_blocks] ((max, sum exp)
+// per row and 128/256-column block), tgt: fp32 [M] (logit of the row's label
+// where the label falls in this GEMM's columns [vocab_off, vocab_off + N)).
+void gemm_ce_stats(torch::Tensor h, torch::Tensor w, torch::Tensor labels, torch::Tensor stats, torch::Tensor tgt,
+                   int64_t vocab_off, int64_t vocab_total, int64_t ignore) {
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous() && labels.numel() == h.size(0),
+              "ce: int64 labels [M]");
+  TORCH_CHECK(tgt.scalar_type() == at::kFloat && tgt.numel() == h.size(0), "ce: fp32 target logits [M]");
+  dtb_ce_check_stats_shape(stats, h.size(0), w.size(0));
+  CeCfg c{labels.data_ptr<int64_t>(), (long)vocab_off, (long)vocab_total, (long)ignore, stats.data_ptr<float>(),
+          tgt.data_ptr<float>(), nullptr, nullptr};
+  gemm_impl(h, w, stats, false, false, dtb::EPI_CE_STATS, c10::nullopt, c10::nullopt, c10::nullopt, c10::nullopt,
+            c10::nullopt, 0, 0, nullptr, &c);
+}
+
+// Fused LM-head cross-entropy, backward half: out[M, N] (bf16) =
+// (softmax(h W^T) - onehot(label)) * dloss * inv_n for the vocabulary columns
+// [vocab_off, vocab_off + N) of w's rows, with lse the full-vocabulary
+// log-sum-exp of each row from the forward.
+void gemm_ce_grad(torch::Tensor h, torch::Tensor w, torch::Tensor labels, torch::Tensor lse, torch::Tensor dloss,
+                  torch::Tensor inv_n, torch::Tensor out, int64_t vocab_off, int64_t vocab_total, int64_t ignore) {
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous() && labels.numel() == h.size(0),
+              "ce: int64 labels [M]");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.numel() == h.size(0), "ce: fp32 lse [M]");
+  TORCH_CHECK(inv_n.scalar_type() == at::kFloat && inv_n.is_cuda(), "ce: fp32 device scalar 1/n");
+  CeCfg c{labels.data_ptr<int64_t>(), (long)vocab_off, (long)vocab_total, (long)ignore, nullptr, nullptr,
+          lse.data_ptr<float>(), inv_n.data_ptr<float>()};
+  gemm_impl(h, w, out, false, false, dtb::EPI_CE_GRAD, c10::nullopt, dloss, c10::nullopt, c10::nullopt,
+            c10::nullopt, 0, 0, nullptr, &c);
 }

@@ -26,6 +26,7 @@ EPI_ACC_F32 = 2      # D(fp32) += acc
 EPI_RESIDUAL = 3     # D = acc + R
 EPI_ROPE = 4         # D = acc with rotate-half RoPE on the first p0 columns, heads of p1
 EPI_SWIGLU = 5       # D = silu(g) * u ; D2 = [g | u]  (g, u: 128-column tiles of B rows n and n+p0)
+EPI_ACC_BF16OUT = 9  # D(bf16) = acc + R(fp32)  (last step of a GEMM chunked over K)
 
 
 def _check_cuda(*ts: torch.Tensor) -> None:

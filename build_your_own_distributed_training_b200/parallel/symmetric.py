@@ -312,6 +312,19 @@ class TPComm:
 
     _sequence_parallel = False
 
+    # per-row records exchanged by the fused vocabulary-parallel cross-entropy
+    def exchange_rows(self, rows: int, row_bytes: int) -> tuple[int, torch.Tensor]:
+        """A staging slot for ``rows`` records of ``row_bytes`` (a multiple of 4): (offset, fp32 view)."""
+        off = self._slot()
+        if rows * row_bytes > self.max_elems * 2:
+            raise ValueError(f"TP staging holds {self.max_elems * 2} bytes, {rows * row_bytes} requested")
+        return off, self.heap.view(off, rows * row_bytes // 4, torch.float32)
+
+    def exchange_publish(self, off: int, rows: torch.Tensor) -> tuple[list[int], int]:
+        """After every rank filled its slot: (heap base of every rank, offset) to read them at."""
+        self.barrier()
+        return self.heap.bases, off
+
     # standalone collectives on bf16 activations
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         x = x.contiguous()

@@ -368,12 +368,18 @@ def vocab_parallel_head_ce(h2: torch.Tensor, weight: torch.Tensor, labels: torch
     """Column-parallel head (rows = this rank's vocab slice) + vocab-parallel CE."""
     assert tp is not None
     x = column_input(h2, tp)
-    logits = linear(x, weight, main_grad=main_grad)
     if labels is None:
-        return logits, None
+        return linear(x, weight, main_grad=main_grad), None
     # every TP rank holds the full batch's labels; under SP the column input
-    # all-gathered the token rows, so logits cover all tokens as well
+    # all-gathered the token rows, so the rows cover all tokens as well
     lab = labels.reshape(-1)
+    if x.is_cuda and weight.shape[0] % 8 == 0:
+        # fused: no logits; the per-row (max, sum exp, target) records cross the TP group
+        from ..ops.loss import NcclRowExchange, fused_head_cross_entropy
+        comm = tp.comm if (tp.fused and tp.comm is not None) else NcclRowExchange(tp.group)
+        return None, fused_head_cross_entropy(x, weight, lab, main_grad=main_grad, vocab_off=vocab_start,
+                                              vocab_total=weight.shape[0] * tp.size, comm=comm)
+    logits = linear(x, weight, main_grad=main_grad)
     return None, _VocabParallelCE.apply(logits, lab, vocab_start, tp.group)
 
 

@@ -238,6 +238,77 @@ def test_cross_entropy(M, V):
     assert _rel(dlog, lr.grad) < 1e-2
 
 
+@pytest.mark.parametrize("M,V,d,chunk", [(512, 32000, 256, 8192), (384, 128256, 128, 8192), (200, 1000, 64, 256),
+                                         (256, 4096, 128, 100000)])
+def test_fused_head_cross_entropy(M, V, d, chunk):
+    """Head GEMM + CE without logits vs the fp32 oracle F.cross_entropy(h W^T)."""
+    from build_your_own_distributed_training_b200.ops import loss as L
+    torch.manual_seed(0)
+    h = _rand(M, d)
+    w = _rand(V, d, scale=0.5)
+    labels = torch.randint(0, V, (M,), device=DEV)
+    labels[::7] = -100
+    labels[0] = V - 1  # last column of the last chunk / block
+    loss, lse, inv_n = L.fused_ce_forward(h, w, labels, 0, V)
+    hf, wf = h.float().requires_grad_(), w.float().requires_grad_()
+    logits = hf @ wf.t()
+    ref = F.cross_entropy(logits, labels, ignore_index=-100)
+    ref.backward()
+    assert abs(float(loss) - float(ref)) < 2e-4 * max(1.0, float(ref))
+    assert _rel(lse, torch.logsumexp(logits.detach(), dim=1)) < 1e-5
+    assert abs(float(inv_n) - 1.0 / int((labels != -100).sum())) < 1e-9
+    dloss = torch.full((), 0.75, device=DEV)
+    dh, dw = L.fused_ce_backward(h, w, labels, lse, inv_n, dloss, 0, V, None, chunk=chunk)
+    assert _rel(dh, 0.75 * hf.grad) < 2e-2
+    assert _rel(dw, 0.75 * wf.grad) < 2e-2
+    # into a main_grad slice: overwritten while fresh, accumulated afterwards
+    mg = torch.full((V * d,), 3.0, device=DEV)
+    from build_your_own_distributed_training_b200.ops import grad_state
+    fs = grad_state.FreshSet(mg)
+    fs.mark([(0, V * d)])
+    grad_state.tag(mg, fs, 0)
+    _, none = L.fused_ce_backward(h, w, labels, lse, inv_n, dloss, 0, V, mg, chunk=chunk)
+    assert none is None and _rel(mg.view(V, d), 0.75 * wf.grad) < 2e-2
+    L.fused_ce_backward(h, w, labels, lse, inv_n, dloss, 0, V, mg, chunk=chunk)
+    assert _rel(mg.view(V, d), 1.5 * wf.grad) < 2e-2
+
+
+def test_fused_head_cross_entropy_vocab_split_matches_whole():
+    """Two vocabulary halves combined through the row-record exchange equal the whole-vocabulary loss."""
+    from build_your_own_distributed_training_b200.ops import loss as L
+    torch.manual_seed(1)
+    M, V, d = 300, 2048, 128
+    h, w = _rand(M, d), _rand(V, d, scale=0.5)
+    labels = torch.randint(0, V, (M,), device=DEV)
+    labels[::5] = -100
+    loss, lse, inv_n = L.fused_ce_forward(h, w, labels, 0, V)
+
+    class TwoHalves:  # both "ranks" on one GPU: records of half 0 and half 1 side by side
+        def __init__(self):
+            self.buf = torch.zeros(2, M * 4, device=DEV)
+            self.r = 0
+
+        def exchange_rows(self, rows, nb):
+            return 0, self.buf[self.r]
+
+        def exchange_publish(self, off, rows):
+            return [self.buf[0].data_ptr(), self.buf[1].data_ptr()], 0
+
+    ex = TwoHalves()
+    ex.r = 1
+    L.fused_ce_forward(h, w[V // 2:], labels, V // 2, V, ex)  # fills half 1's records
+    ex.r = 0
+    loss0, lse0, inv0 = L.fused_ce_forward(h, w[:V // 2], labels, 0, V, ex)
+    assert abs(float(loss0) - float(loss)) < 1e-5 * max(1.0, float(loss))
+    assert _rel(lse0, lse) < 1e-6 and float(inv0) == float(inv_n)
+    dloss = torch.ones((), device=DEV)
+    dh, dw = L.fused_ce_backward(h, w, labels, lse, inv_n, dloss, 0, V, None)
+    dh0, dw0 = L.fused_ce_backward(h, w[:V // 2], labels, lse0, inv0, dloss, 0, V, None)
+    dh1, dw1 = L.fused_ce_backward(h, w[V // 2:], labels, lse0, inv0, dloss, V // 2, V, None)
+    assert _rel(dh0.float() + dh1.float(), dh) < 1e-2
+    assert _rel(torch.cat([dw0, dw1]), dw) < 1e-3
+
+
 def test_adamw_matches_torch():
     n = 100_003
     p = torch.randn(n, device=DEV)
