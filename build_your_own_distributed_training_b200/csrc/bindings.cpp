@@ -16,6 +16,7 @@ std::vector<torch::Tensor> cross_entropy_fwd(torch::Tensor logits, torch::Tensor
 void adamw(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, torch::Tensor out,
            c10::optional<torch::Tensor> clip, double lr, double b1, double b2, double eps, double wd, int64_t step);
 torch::Tensor sumsq(torch::Tensor x);
+torch::Tensor sum_small(torch::Tensor x);
 std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t B, int64_t S, int64_t nq, int64_t nkv, int64_t hd,
                                     double scale, bool legacy);
 torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, int64_t B, int64_t S,
@@ -23,7 +24,7 @@ torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qkv, torch::Tensor o, tor
 int64_t device_error();
 void gemm_peer_ar(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool b_mn, c10::optional<torch::Tensor> R,
                   c10::optional<torch::Tensor> alpha, std::vector<int64_t> bases, int64_t rank, int64_t stage_off,
-                  int64_t flag_off, int64_t epoch, double timeout_s);
+                  int64_t flag_off, int64_t epoch, double timeout_s, bool two_shot);
 void gemm_peer_rs(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool b_mn, c10::optional<torch::Tensor> R,
                   std::vector<int64_t> bases, int64_t rank, int64_t stage_off, int64_t flag_off, int64_t epoch,
                   double timeout_s, int64_t row0, int64_t rows);
@@ -33,8 +34,9 @@ int64_t ipc_open(torch::Tensor handle);
 void ipc_close(int64_t ptr);
 void peer_barrier(std::vector<int64_t> bases, int64_t flag_off, int64_t rank, int64_t epoch, double timeout_s);
 void peer_all_gather(std::vector<int64_t> bases, int64_t src_off, int64_t shard_bytes, torch::Tensor out);
-torch::Tensor peer_reduce_scatter(std::vector<int64_t> bases, int64_t grad_off, int64_t rank, double scale,
-                                  torch::Tensor out);
+int64_t reduce_scatter_blocks(int64_t n);
+void peer_reduce_scatter(std::vector<int64_t> bases, int64_t grad_off, int64_t rank, double scale, torch::Tensor out,
+                         c10::optional<torch::Tensor> part, int64_t split, double rep_w);
 void peer_all_reduce_bf16(std::vector<int64_t> bases, int64_t src_off, c10::optional<torch::Tensor> residual,
                           torch::Tensor out);
 void peer_reduce_rows_bf16(std::vector<int64_t> bases, int64_t src_off, int64_t row0, int64_t cols, torch::Tensor out);
@@ -65,12 +67,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cross_entropy_fwd", &cross_entropy_fwd);
   m.def("adamw", &adamw);
   m.def("sumsq", &sumsq);
+  m.def("sum_small", &sum_small, "fixed-order sum of a small fp32 buffer");
   m.def("attn_fwd", &attn_fwd, py::arg("qkv"), py::arg("B"), py::arg("S"), py::arg("nq"), py::arg("nkv"),
         py::arg("hd"), py::arg("scale"), py::arg("legacy") = false);
   m.def("attn_bwd", &attn_bwd, py::arg("dO"), py::arg("qkv"), py::arg("o"), py::arg("lse"), py::arg("B"),
         py::arg("S"), py::arg("nq"), py::arg("nkv"), py::arg("hd"), py::arg("scale"), py::arg("legacy") = false);
   m.def("device_error", &device_error, "read and clear the device error word");
-  m.def("gemm_peer_ar", &gemm_peer_ar, "tcgen05 GEMM fused with an NVLink all-reduce over the peer group");
+  m.def("gemm_peer_ar", &gemm_peer_ar, "tcgen05 GEMM fused with an NVLink all-reduce over the peer group",
+        py::arg("A"), py::arg("B"), py::arg("D"), py::arg("b_mn"), py::arg("R"), py::arg("alpha"), py::arg("bases"),
+        py::arg("rank"), py::arg("stage_off"), py::arg("flag_off"), py::arg("epoch"), py::arg("timeout_s"),
+        py::arg("two_shot") = false);
   m.def("gemm_peer_rs", &gemm_peer_rs, "tcgen05 GEMM fused with an NVLink reduce-scatter of rows over the peer group");
   m.def("sym_malloc", &sym_malloc, "raw device allocation for a symmetric heap");
   m.def("ipc_handle", &ipc_handle);
@@ -78,7 +84,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &ipc_close);
   m.def("peer_barrier", &peer_barrier);
   m.def("peer_all_gather", &peer_all_gather);
-  m.def("peer_reduce_scatter", &peer_reduce_scatter);
+  m.def("peer_reduce_scatter", &peer_reduce_scatter, py::arg("bases"), py::arg("grad_off"), py::arg("rank"),
+        py::arg("scale"), py::arg("out"), py::arg("part") = py::none(), py::arg("split") = 0, py::arg("rep_w") = 1.0);
+  m.def("reduce_scatter_blocks", &reduce_scatter_blocks);
   m.def("peer_all_reduce_bf16", &peer_all_reduce_bf16);
   m.def("peer_reduce_rows_bf16", &peer_reduce_rows_bf16);
   m.def("wait_flag_probe", &wait_flag_probe, "bounded wait on a flag (tests the timeout path)");

@@ -60,10 +60,14 @@ __global__ void peer_all_gather_kernel(PeerPtrs peers, long src_off, long shard_
 
 // ---------------------------------------------------------------- reduce-scatter
 // out[i] = scale * sum_{p = 0..size-1} grad_p[rank * n + i]   (fp32, fixed order)
-// also leaves the sum of squares of out in part[blockIdx.x] (for the grad norm).
+// and, for the gradient norm, part[blockIdx.x] = sum_i w_i * out[i]^2 with
+// w_i = 1 below `split` (TP-sharded entries) and rep_w from there on
+// (TP-replicated entries, which every TP rank holds: rep_w = 1/tp), so the
+// norm needs no second pass over the shard.
 template <int NT>
 __global__ void __launch_bounds__(NT) peer_reduce_scatter_kernel(PeerPtrs peers, long grad_off, long n, int rank,
-                                                                int size, float scale, float* out, float* part) {
+                                                                int size, float scale, float* out, float* part,
+                                                                long split, float rep_w) {
   __shared__ float red[32];
   float ss = 0.f;
   const long nv = n / 4;
@@ -79,7 +83,15 @@ __global__ void __launch_bounds__(NT) peer_reduce_scatter_kernel(PeerPtrs peers,
     }
     acc.x *= scale; acc.y *= scale; acc.z *= scale; acc.w *= scale;
     reinterpret_cast<float4*>(out)[i] = acc;
-    ss += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
+    const long e = i * 4;
+    if (e + 4 <= split) {
+      ss += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
+    } else if (e >= split) {
+      ss += rep_w * (acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w);
+    } else {
+      ss += (e < split ? 1.f : rep_w) * acc.x * acc.x + (e + 1 < split ? 1.f : rep_w) * acc.y * acc.y +
+            (e + 2 < split ? 1.f : rep_w) * acc.z * acc.z + (e + 3 < split ? 1.f : rep_w) * acc.w * acc.w;
+    }
   }
   // per-block partial of sum(out^2), fixed order
   float v = warp_sum(ss);
@@ -230,19 +242,28 @@ void peer_all_gather(std::vector<int64_t> bases, int64_t src_off, int64_t shard_
   DTB_LAUNCH_CHECK();
 }
 
-// returns the per-block sum-of-squares partials of the result
-torch::Tensor peer_reduce_scatter(std::vector<int64_t> bases, int64_t grad_off, int64_t rank, double scale,
-                                  torch::Tensor out) {
+// Reduce-scatter (mean over the group) of an fp32 gradient buffer.  `part`
+// (optional, fp32, at least reduce_scatter_blocks(n) entries) receives the
+// per-block weighted sums of squares of the result (see the kernel); entries
+// past the blocks used are left untouched.
+int64_t reduce_scatter_blocks(int64_t n) { return blocks_for(n / 4, 256); }
+
+void peer_reduce_scatter(std::vector<int64_t> bases, int64_t grad_off, int64_t rank, double scale, torch::Tensor out,
+                         c10::optional<torch::Tensor> part, int64_t split, double rep_w) {
   DTB_CHECK(out.scalar_type() == at::kFloat && out.is_contiguous(), "reduce-scatter: fp32 shard");
   const long n = out.numel();
   DTB_CHECK(n % 4 == 0 && grad_off % 16 == 0, "reduce-scatter needs 16-byte aligned shards");
   auto peers = make_peers(bases);
   const int nb = blocks_for(n / 4, 256);
-  auto part = torch::zeros({nb}, out.options());
+  float* pp = nullptr;
+  if (part.has_value()) {
+    DTB_CHECK(part->scalar_type() == at::kFloat && part->is_contiguous() && part->numel() >= nb,
+              "reduce-scatter: partials need %d fp32 entries", nb);
+    pp = part->data_ptr<float>();
+  }
   peer_reduce_scatter_kernel<256><<<nb, 256, 0, cs()>>>(peers, grad_off, n, (int)rank, (int)bases.size(), (float)scale,
-                                                        out.data_ptr<float>(), part.data_ptr<float>());
+                                                        out.data_ptr<float>(), pp, (long)split, (float)rep_w);
   DTB_LAUNCH_CHECK();
-  return part;
 }
 
 void peer_all_reduce_bf16(std::vector<int64_t> bases, int64_t src_off, c10::optional<torch::Tensor> residual,

@@ -855,6 +855,16 @@ void adamw(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, t
   DTB_LAUNCH_CHECK();
 }
 
+// Fixed-order sum of a small fp32 buffer (per-block partials) in one CTA.
+torch::Tensor sum_small(torch::Tensor x) {
+  TORCH_CHECK(x.scalar_type() == at::kFloat && x.is_contiguous() && x.numel() < (1L << 31), "sum_small: fp32");
+  const c10::cuda::CUDAGuard g(x.device());
+  auto out = torch::empty({}, x.options());
+  sum_parts_kernel<1024><<<1, 1024, 0, cur_stream()>>>(x.data_ptr<float>(), (int)x.numel(), out.data_ptr<float>());
+  DTB_LAUNCH_CHECK();
+  return out;
+}
+
 torch::Tensor sumsq(torch::Tensor x) {
   TORCH_CHECK(x.scalar_type() == at::kFloat && x.is_contiguous(), "sumsq: contiguous fp32");
   const c10::cuda::CUDAGuard g(x.device());

@@ -75,6 +75,7 @@ struct GemmArgs {
   uint8_t* peer_base[MAX_PEERS];
   int peer_n, peer_rank;
   int rs_row0, rs_rows;  // rs_rows > 0: reduce-scatter, this rank sums rows [rs_row0, rs_row0 + rs_rows) only
+  int two_shot;          // all-reduce in two steps: each tile's owner sums it, the others copy the sum
   long stage_off, flag_off;
   uint32_t epoch;
   uint64_t timeout_ns;
@@ -192,10 +193,16 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
     const int c0 = nb * 128;
 #pragma unroll 1
     for (int c = 0; c < 128; c += 32) {
-      float g[32], u[32];
-      tmem_ld32(trow + c, g);
-      tmem_ld32(trow + 128 + c, u);
+      uint32_t rg[32], ru[32];
+      tmem_ld32_async(trow + c, rg);
+      tmem_ld32_async(trow + 128 + c, ru);
+      tmem_wait_ld();
+      tmem_regs(rg);
+      tmem_regs(ru);
       if (row_ok) {
+        float g[32], u[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) g[i] = __uint_as_float(rg[i]), u[i] = __uint_as_float(ru[i]);
         __nv_bfloat16* gp = a.D2 + (long)row * a.ldd2 + c0 + c;
         __nv_bfloat16* up = gp + a.ffn;
         // the backward recomputes from the rounded g/u, so round first
@@ -204,7 +211,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
         for (int i = 0; i < 32; ++i) {
           gr[i] = __bfloat162float(__float2bfloat16_rn(g[i]));
           ur[i] = __bfloat162float(__float2bfloat16_rn(u[i]));
-          h[i] = gr[i] / (1.f + __expf(-gr[i])) * ur[i];
+          h[i] = __fdividef(gr[i], 1.f + __expf(-gr[i])) * ur[i];
         }
         store_bf16_32(gp, gr);
         store_bf16_32(up, ur);
@@ -305,7 +312,10 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
   const int n0 = nb * BN;
   if (EPI == EPI_ROPE) {
     const int hd = a.head_dim, half = hd >> 1;
+    // this row's table rows (pos < seqlen also for rows past M, which are not stored)
     const int pos = row % a.seqlen;
+    const float4* crow = reinterpret_cast<const float4*>(a.cos_t + (long)pos * hd);
+    const float4* srow = reinterpret_cast<const float4*>(a.sin_t + (long)pos * hd);
 #pragma unroll 1
     for (int h0 = 0; h0 < BN; h0 += hd) {
       const int col = n0 + h0;
@@ -313,18 +323,29 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
       if (col < a.rope_cols) {
 #pragma unroll 1
         for (int j = 0; j < half; j += 32) {
-          float x1[32], x2[32];
-          tmem_ld32(trow + h0 + j, x1);
-          tmem_ld32(trow + h0 + half + j, x2);
+          // table loads first, then both TMEM loads under one wait: the L2 and
+          // TMEM latencies overlap instead of adding up
+          float4 c4[8], s4[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            c4[q] = __ldg(crow + (j >> 2) + q);
+            s4[q] = __ldg(srow + (j >> 2) + q);
+          }
+          uint32_t r1[32], r2[32];
+          tmem_ld32_async(trow + h0 + j, r1);
+          tmem_ld32_async(trow + h0 + half + j, r2);
+          tmem_wait_ld();
+          tmem_regs(r1);
+          tmem_regs(r2);
           if (row_ok) {
-            const float* cs = a.cos_t + (long)pos * hd + j;
-            const float* sn = a.sin_t + (long)pos * hd + j;
+            const float* cs = reinterpret_cast<const float*>(c4);
+            const float* sn = reinterpret_cast<const float*>(s4);
             float y1[32], y2[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-              const float c = cs[i], s = sn[i];
-              y1[i] = x1[i] * c - x2[i] * s;
-              y2[i] = x2[i] * c + x1[i] * s;
+              const float x1 = __uint_as_float(r1[i]), x2 = __uint_as_float(r2[i]);
+              y1[i] = x1 * cs[i] - x2 * sn[i];
+              y2[i] = x2 * cs[i] + x1 * sn[i];
             }
             __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(a.D) + (long)row * a.ldd + col + j;
             store_bf16_32(p, y1);
@@ -333,10 +354,21 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
         }
       } else {
 #pragma unroll 1
-        for (int j = 0; j < hd; j += 32) {
-          float x[32];
-          tmem_ld32(trow + h0 + j, x);
-          if (row_ok) store_chunk<EPI_STORE_BF16>(a, row, col + j, x, 32);
+        for (int j = 0; j < hd; j += 64) {
+          uint32_t r1[32], r2[32];
+          tmem_ld32_async(trow + h0 + j, r1);
+          tmem_ld32_async(trow + h0 + j + 32, r2);
+          tmem_wait_ld();
+          tmem_regs(r1);
+          tmem_regs(r2);
+          if (row_ok) {
+            float v1[32], v2[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v1[i] = __uint_as_float(r1[i]), v2[i] = __uint_as_float(r2[i]);
+            __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(a.D) + (long)row * a.ldd + col + j;
+            store_bf16_32(p, v1);
+            store_bf16_32(p + 32, v2);
+          }
         }
       }
     }
@@ -394,7 +426,7 @@ __device__ __forceinline__ void peer_ar_publish(const GemmArgs& a, int tile, int
 // and of the residual are all issued before any is used (NP * RU + RU 16-byte
 // loads in flight per lane), so a step costs one NVLink round trip; the sum
 // then runs in rank order, which keeps every rank's result bitwise equal.
-template <int NP, int RU>
+template <int NP, int RU, bool WRITEBACK = false>
 __device__ __forceinline__ void peer_sum_rows(const GemmArgs& a, int row0, int n0, int c) {
 #pragma unroll 1
   for (int r = 0; r < 32; r += RU) {
@@ -447,6 +479,8 @@ __device__ __forceinline__ void peer_sum_rows(const GemmArgs& a, int row0, int n
       o.z = pack_bf16x2(acc[4], acc[5]);
       o.w = pack_bf16x2(acc[6], acc[7]);
       *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.D) + (long)(rr - a.rs_row0) * a.ldd + n0 + c) = o;
+      if (WRITEBACK)  // two-shot owner: the sum replaces this rank's staged partial, for the peers to copy
+        *reinterpret_cast<uint4*>(a.peer_base[a.peer_rank] + a.stage_off + ((long)rr * a.ldd + n0 + c) * 2) = o;
     }
   }
 }
@@ -475,6 +509,74 @@ __device__ __forceinline__ bool peer_ar_finish(const GemmArgs& a, int tile, int 
   if (a.peer_n <= 2) peer_sum_rows<2, 8>(a, row0, n0, c);
   else if (a.peer_n <= 4) peer_sum_rows<4, 4>(a, row0, n0, c);
   else peer_sum_rows<8, 2>(a, row0, n0, c);
+  return true;
+}
+
+// ---------------------------------------------------------------- two-shot all-reduce
+// For larger TP groups the one-shot finish above pulls (tp - 1) copies of every
+// tile into every rank.  Two-shot: the (tile, quadrant) flag unit `f` belongs
+// to rank f % tp.  Its owner waits for every rank's staged partial, sums them in
+// rank order (+ residual) into D and back into its own staging slot, then
+// raises a "done" flag in every peer's heap; the other ranks copy the sum from
+// the owner.  Per-rank NVLink ingress drops from (tp-1) to 2(tp-1)/tp payloads.
+// Done flags follow the partial flags: done_off = flag_off + peer_n * nflags * 4.
+__device__ __forceinline__ int two_shot_owner(const GemmArgs& a, int tile, int quad) {
+  return (int)(((long)tile * 4 + quad) % a.peer_n);
+}
+
+template <int BN>
+__device__ __forceinline__ bool peer_ar_reduce_own(const GemmArgs& a, int tile, int mb, int nb, int quad, int lane) {
+  const long nflags = (long)a.flag_tiles * 4;
+  const long f = (long)tile * 4 + quad;
+  const uint32_t* mine = reinterpret_cast<const uint32_t*>(a.peer_base[a.peer_rank] + a.flag_off);
+  bool ok = true;
+  for (int p = 0; p < a.peer_n && ok; ++p) ok = wait_flag(mine + (long)p * nflags + f, a.epoch, a.timeout_ns, a.err);
+  if (!ok) return false;
+  const int row0 = mb * BM + quad * 32;
+  const int n0 = nb * BN;
+  const int cols = min(BN, a.N - n0);
+  const int c = lane * 8;
+  if (c < cols) {
+    if (a.peer_n <= 4) peer_sum_rows<4, 4, true>(a, row0, n0, c);
+    else peer_sum_rows<8, 2, true>(a, row0, n0, c);
+  }
+  const long done_off = a.flag_off + (long)a.peer_n * nflags * 4;
+  __syncwarp();
+  if (lane < a.peer_n && lane != a.peer_rank)
+    st_release_sys(reinterpret_cast<uint32_t*>(a.peer_base[lane] + done_off) + f, a.epoch);
+  return true;
+}
+
+template <int BN>
+__device__ __forceinline__ bool peer_ar_fetch(const GemmArgs& a, int tile, int mb, int nb, int quad, int lane) {
+  const long nflags = (long)a.flag_tiles * 4;
+  const long f = (long)tile * 4 + quad;
+  const int owner = two_shot_owner(a, tile, quad);
+  const long done_off = a.flag_off + (long)a.peer_n * nflags * 4;
+  if (!wait_flag(reinterpret_cast<const uint32_t*>(a.peer_base[a.peer_rank] + done_off) + f, a.epoch, a.timeout_ns,
+                 a.err))
+    return false;
+  const int row0 = mb * BM + quad * 32;
+  const int n0 = nb * BN;
+  const int cols = min(BN, a.N - n0);
+  const int c = lane * 8;
+  if (c >= cols) return true;
+  const uint8_t* src = a.peer_base[owner] + a.stage_off;
+  constexpr int RU = 8;
+#pragma unroll 1
+  for (int r = 0; r < 32; r += RU) {
+    uint4 v[RU];
+#pragma unroll
+    for (int i = 0; i < RU; ++i) {
+      const int rr = row0 + r + i;
+      v[i] = rr < a.M ? ld_cg_v4(src + ((long)rr * a.ldd + n0 + c) * 2) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int i = 0; i < RU; ++i) {
+      const int rr = row0 + r + i;
+      if (rr < a.M) *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.D) + (long)rr * a.ldd + n0 + c) = v[i];
+    }
+  }
   return true;
 }
 
@@ -659,6 +761,7 @@ __global__ void __launch_bounds__(320, 1)
     const int wg = (warp - 2) >> 2;
     int t = 0;
     int pend_tile = -1, pend_mb = 0, pend_nb = 0;  // EPI_PEER_AR: tile published, not yet reduced
+    int pend2_tile = -1, pend2_mb = 0, pend2_nb = 0;  // two-shot: reduced by its owner, not yet copied
     for (int tile = unit; tile < args.num_tiles; tile += units, ++t) {
       const int acc = t & 1;
       if (acc != wg) continue;
@@ -686,7 +789,22 @@ __global__ void __launch_bounds__(320, 1)
       }
       if constexpr (EPI == EPI_PEER_AR) {
         peer_ar_publish(args, ftile, quad, lane);
-        if (pend_tile >= 0 && !peer_ar_finish<BN>(args, pend_tile, pend_mb, pend_nb, quad, lane)) {
+        if (args.two_shot) {
+          // tile k-1: its owner sums it; tile k-2: the others copy the owner's sum
+          bool ok = true;
+          if (pend_tile >= 0 && two_shot_owner(args, pend_tile, quad) == args.peer_rank)
+            ok = peer_ar_reduce_own<BN>(args, pend_tile, pend_mb, pend_nb, quad, lane);
+          if (ok && pend2_tile >= 0 && two_shot_owner(args, pend2_tile, quad) != args.peer_rank)
+            ok = peer_ar_fetch<BN>(args, pend2_tile, pend2_mb, pend2_nb, quad, lane);
+          if (!ok) {
+            *abort_flag = 1;
+            pend_tile = pend2_tile = -1;
+            break;
+          }
+          pend2_tile = pend_tile;
+          pend2_mb = pend_mb;
+          pend2_nb = pend_nb;
+        } else if (pend_tile >= 0 && !peer_ar_finish<BN>(args, pend_tile, pend_mb, pend_nb, quad, lane)) {
           *abort_flag = 1;
           pend_tile = -1;
           break;
@@ -697,7 +815,18 @@ __global__ void __launch_bounds__(320, 1)
       }
     }
     if constexpr (EPI == EPI_PEER_AR) {
-      if (pend_tile >= 0 && !peer_ar_finish<BN>(args, pend_tile, pend_mb, pend_nb, quad, lane)) *abort_flag = 1;
+      if (args.two_shot) {
+        bool ok = true;
+        if (pend_tile >= 0 && two_shot_owner(args, pend_tile, quad) == args.peer_rank)
+          ok = peer_ar_reduce_own<BN>(args, pend_tile, pend_mb, pend_nb, quad, lane);
+        if (ok && pend2_tile >= 0 && two_shot_owner(args, pend2_tile, quad) != args.peer_rank)
+          ok = peer_ar_fetch<BN>(args, pend2_tile, pend2_mb, pend2_nb, quad, lane);
+        if (ok && pend_tile >= 0 && two_shot_owner(args, pend_tile, quad) != args.peer_rank)
+          ok = peer_ar_fetch<BN>(args, pend_tile, pend_mb, pend_nb, quad, lane);
+        if (!ok) *abort_flag = 1;
+      } else if (pend_tile >= 0 && !peer_ar_finish<BN>(args, pend_tile, pend_mb, pend_nb, quad, lane)) {
+        *abort_flag = 1;
+      }
     }
   }
   tc_fence_before();
@@ -839,6 +968,7 @@ struct PeerCfg {
   uint32_t epoch;
   double timeout_s;
   int rs_row0 = 0, rs_rows = 0;  // reduce-scatter: this rank's output rows
+  bool two_shot = false;
 };
 
 // Fused LM-head cross-entropy epilogues (EPI_CE_STATS / EPI_CE_GRAD).
@@ -887,6 +1017,7 @@ static void gemm_impl(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_
     g.timeout_ns = (uint64_t)(peer->timeout_s * 1e9);
     g.rs_row0 = peer->rs_row0;
     g.rs_rows = peer->rs_rows;
+    g.two_shot = peer->two_shot && peer->rs_rows == 0 && g.peer_n > 1 ? 1 : 0;
     if (g.rs_rows > 0)
       DTB_CHECK(g.rs_row0 % BM == 0 && g.rs_rows % BM == 0 && g.rs_row0 + g.rs_rows <= M && D.size(0) == g.rs_rows,
                 "peer GEMM reduce-scatter: row block [%d, %d) must be 128-row aligned and match D", g.rs_row0,
@@ -946,6 +1077,9 @@ static void gemm_impl(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_
     TORCH_CHECK(cos_t.has_value() && sin_t.has_value(), "gemm: rope tables missing");
     g.cos_t = cos_t->data_ptr<float>();
     g.sin_t = sin_t->data_ptr<float>();
+    TORCH_CHECK(((reinterpret_cast<uintptr_t>(g.cos_t) | reinterpret_cast<uintptr_t>(g.sin_t)) & 15) == 0 &&
+                    cos_t->is_contiguous() && sin_t->is_contiguous(),
+                "gemm: rope tables must be contiguous and 16-byte aligned");
   }
   if (e == EPI_SWIGLU) {
     TORCH_CHECK(D2.has_value(), "gemm: swiglu needs D2");
@@ -1008,10 +1142,13 @@ void gemm_entry(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_mn, bo
 // D = sum over the peer group of (A x B) (+ R): the GEMM fused with an
 // all-reduce through the symmetric heaps (staging at stage_off, flags at
 // flag_off, both inside every rank's heap; epoch increases by one per call).
+// two_shot: see peer_ar_reduce_own; the flag area then holds (peer_n + 1) x flag
+// slots (the partial flags of every rank, then the done flags).
 void gemm_peer_ar(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool b_mn, c10::optional<torch::Tensor> R,
                   c10::optional<torch::Tensor> alpha, std::vector<int64_t> bases, int64_t rank, int64_t stage_off,
-                  int64_t flag_off, int64_t epoch, double timeout_s) {
+                  int64_t flag_off, int64_t epoch, double timeout_s, bool two_shot) {
   PeerCfg pc{bases, (int)rank, (long)stage_off, (long)flag_off, (uint32_t)epoch, timeout_s};
+  pc.two_shot = two_shot;
   gemm_impl(A, B, D, false, b_mn, dtb::EPI_PEER_AR, R, alpha, c10::nullopt, c10::nullopt, c10::nullopt, 0, 0, &pc);
 }
 

@@ -25,14 +25,16 @@ COMM_HINTS = ("nccl", "all_reduce", "allreduce", "all_gather", "allgather", "red
 # over NVLink (all-reduce, or reduce-scatter under sequence parallelism).
 FUSED_HINTS = ("ag_gemm", "gemm_ar", "gemm_rs")
 PEER_EPILOGUE_ID = 6
-_GEMM_TEMPLATE = re.compile(r"gemm_tcgen05_kernel<\s*(\d+)\s*,\s*(\d+)\s*,\s*(\d+)\s*,\s*(\d+)\s*,\s*(\d+)")
+# template arguments as profilers print them: integers, bools as 0/1 or false/true
+_ARG = r"\s*(\w+)\s*"
+_GEMM_TEMPLATE = re.compile(r"gemm_tcgen05_kernel<" + ",".join([_ARG] * 5))
 
 
 def is_fused_comm_kernel(name: str) -> bool:
     """True for a kernel that fuses a collective into its GEMM (by template epilogue id or name)."""
     m = _GEMM_TEMPLATE.search(name)
     if m is not None:
-        return int(m.group(5)) == PEER_EPILOGUE_ID
+        return m.group(5) == str(PEER_EPILOGUE_ID)
     low = name.lower()
     return any(h in low for h in FUSED_HINTS)
 

@@ -182,6 +182,13 @@ class FullyShardedModel(nn.Module):
         self._slot_owner: dict[int, int] = {}
         self._rs_pending: list[Any] = []
         self._bwd_started = False
+        # transports whose reduce-scatter also yields the gradient-norm partials
+        # (per unit, per block; zero where a unit uses fewer blocks)
+        self._norm_parts: torch.Tensor | None = None
+        self._norm_fresh = [False] * len(self.units)
+        if getattr(self.comm, "norm_partials", False) and self.units and self.replication == 1:
+            nb = max(self.comm.norm_partial_blocks(u.shard_numel) for u in self.units)
+            self._norm_parts = torch.zeros(len(self.units), nb, device=self.device, dtype=torch.float32)
         self._gather_all_root()
 
     # ------------------------------------------------------------------ build
@@ -403,7 +410,14 @@ class FullyShardedModel(nn.Module):
             rep = u.grad[u.tp_end:]
             self.comm.all_reduce_sum(rep, self.tp_group) if not hasattr(self.comm, "tp_all_reduce") \
                 else self.comm.tp_all_reduce(rep)
-        self.comm.reduce_scatter_mean(u.grad_shard, u.grad, self.dp_size)
+        if self._norm_parts is not None:
+            lo, hi = u.shard_range(self.shard_rank)
+            split = min(max(u.tp_end - lo, 0), hi - lo)  # shard-local start of the TP-replicated entries
+            self.comm.reduce_scatter_mean(u.grad_shard, u.grad, self.dp_size, part=self._norm_parts[u.index],
+                                          split=split, rep_w=1.0 / self.tp_size)
+            self._norm_fresh[u.index] = True
+        else:
+            self.comm.reduce_scatter_mean(u.grad_shard, u.grad, self.dp_size)
 
     def wait_reduce(self) -> None:
         if self._is_cuda:
@@ -420,6 +434,7 @@ class FullyShardedModel(nn.Module):
 
     def zero_grad_buffers(self) -> None:
         """Logically zero every gradient: slices become fresh, the first writer overwrites them."""
+        self._norm_fresh = [False] * len(self.units)
         for u in self.units:
             u.fresh.mark([(e.offset, e.numel) for e in u.entries])
 
@@ -432,7 +447,13 @@ class FullyShardedModel(nn.Module):
         return [(u, *u.shard_range(self.shard_rank)) for u in self.units]
 
     def grad_norm_sq_local(self) -> torch.Tensor:
-        """Sum of g^2 over this rank's gradient shards; TP-replicated entries weighted 1/tp."""
+        """Sum of g^2 over this rank's gradient shards; TP-replicated entries weighted 1/tp.
+
+        When this step's reduce-scatters left their per-block partials (NVLink transport),
+        this is one fixed-order sum over them; otherwise a pass over the shards."""
+        if self._norm_parts is not None and all(self._norm_fresh):
+            from ..ops._ext import native
+            return native().sum_small(self._norm_parts)
         tot = torch.zeros((), dtype=torch.float32, device=self.device)
         for u in self.units:
             lo, hi = u.shard_range(self.shard_rank)

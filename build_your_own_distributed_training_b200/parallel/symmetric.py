@@ -164,11 +164,21 @@ class PeerComm:
         nbytes = shard.numel() * shard.element_size()
         native().peer_all_gather(self.heap.bases, self.heap.offset_of(shard), nbytes, out_full)
 
-    def reduce_scatter_mean(self, out_shard: torch.Tensor, full: torch.Tensor, world: int) -> torch.Tensor:
+    # the reduce-scatter also leaves per-block partial sums of squares of its result
+    norm_partials = True
+
+    @staticmethod
+    def norm_partial_blocks(shard_numel: int) -> int:
+        return int(native().reduce_scatter_blocks(shard_numel))
+
+    def reduce_scatter_mean(self, out_shard: torch.Tensor, full: torch.Tensor, world: int,
+                            part: torch.Tensor | None = None, split: int = 0, rep_w: float = 1.0) -> None:
+        """``out_shard = mean over ranks of this rank's slice of full``; with ``part``, also
+        ``part[b] = sum over block b of w_i * out_i^2`` (``w_i = 1`` below ``split``, else ``rep_w``)."""
         assert self.heap is not None
         self._rs_barrier()  # every rank finished accumulating this unit's gradients
-        return native().peer_reduce_scatter(self.heap.bases, self.heap.offset_of(full), self.rank, 1.0 / world,
-                                            out_shard)
+        native().peer_reduce_scatter(self.heap.bases, self.heap.offset_of(full), self.rank, 1.0 / world,
+                                     out_shard, part, split, rep_w)
 
     def all_reduce_sum(self, t: torch.Tensor, group: dist.ProcessGroup | None) -> None:
         dist.all_reduce(t, group=group)
@@ -239,10 +249,15 @@ class TPComm:
         self.rank = dist.get_rank(group)
         self.max_tokens, self.width = max_tokens, width
         self.max_elems = max_tokens * width
-        # one flag per (128-row slab, column block, quadrant, rank); +1 slab row covers
-        # 256-row CTA-pair tiles that overhang max_tokens
+        # one flag per (128-row slab, column block, quadrant, rank), then one "done" flag per
+        # (slab, block, quadrant) for the two-shot all-reduce; +1 slab row covers 256-row
+        # CTA-pair tiles that overhang max_tokens
         tiles = (-(-max_tokens // 128) + 1) * (-(-width // 128))
-        self.flag_bytes = _align(tiles * 4 * self.size * 4)
+        self.flag_bytes = _align(tiles * 4 * (self.size + 1) * 4)
+        # two-shot (owner sums, others copy) once one-shot ingress, (tp-1) payloads per rank,
+        # exceeds two-shot's 2(tp-1)/tp; DTB_TP_TWO_SHOT=0/1 overrides
+        env = os.environ.get("DTB_TP_TWO_SHOT")
+        self.two_shot = (env == "1") if env in ("0", "1") else self.size >= 4
         slot = _align(self.max_elems * 2)
         self.heap = SymmetricHeap(group, 2 * slot + self.flag_bytes + 64 * 1024, device)
         self.slots = [self.heap.alloc(slot), self.heap.alloc(slot)]
@@ -271,7 +286,7 @@ class TPComm:
         out = torch.empty(M, N, device=x2.device, dtype=torch.bfloat16)
         off = self._slot()
         native().gemm_peer_ar(x2, w, out, False, residual, None, self.heap.bases, self.rank, off, self.flag_off,
-                              self.calls, TIMEOUT_S)
+                              self.calls, TIMEOUT_S, self.two_shot)
         return out
 
     # fused input-gradient GEMM -> all-reduce of a column-parallel layer: dy @ W, summed over TP
@@ -283,7 +298,7 @@ class TPComm:
         out = torch.empty(M, K, device=dy.device, dtype=torch.bfloat16)
         off = self._slot()
         native().gemm_peer_ar(dy.contiguous(), w, out, True, None, None, self.heap.bases, self.rank, off,
-                              self.flag_off, self.calls, TIMEOUT_S)
+                              self.flag_off, self.calls, TIMEOUT_S, self.two_shot)
         return out
 
     # fused GEMM -> reduce-scatter of rows (+ residual in the scattered layout)

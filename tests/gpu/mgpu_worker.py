@@ -55,6 +55,15 @@ def main():
     dist.all_gather(every, grad.clone())
     exact = sum(e[rank * n:(rank + 1) * n] for e in every) / world  # same order: rank 0..world-1
     check(torch.equal(out, exact), "peer reduce-scatter is not the fixed-order sum")
+    # its gradient-norm partials: weight 1 below the split, rep_w above (TP-replicated entries)
+    part = torch.zeros(native().reduce_scatter_blocks(n) + 3, device=dev)
+    split = n // 3 + 1
+    pc.reduce_scatter_mean(out, grad, world, part=part, split=split, rep_w=0.5)
+    wts = torch.ones(n, device=dev, dtype=torch.float64)
+    wts[split:] = 0.5
+    ref_ss = float((out.double() ** 2 * wts).sum())
+    check(abs(float(part.double().sum()) - ref_ss) < 1e-5 * ref_ss, "reduce-scatter norm partials differ from fp64")
+    check(float(part[-3:].abs().sum()) == 0.0, "reduce-scatter wrote past its blocks")
 
     # ---- TP transport
     M, K, N = 1024, 512, 768
@@ -103,7 +112,13 @@ def main():
     from build_your_own_distributed_training_b200.training.trainer import Trainer
     root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     results = {}
-    for tp, sp in ((world, False), (world, True), (1, False)):
+    # (tp, sequence parallel, loss parallel): pure TP, TP+SP, pure ZeRO, vocabulary-parallel loss,
+    # and at 4+ GPUs the 2-D layout tp2 x dp(world/2), where the ZeRO pull transport and the
+    # TP-fused GEMMs run in the same step
+    layouts = [(world, False, False), (world, True, False), (1, False, False), (world, False, True)]
+    if world >= 4:
+        layouts += [(2, False, False), (2, True, True)]
+    for tp, sp, lp in layouts:
         ctx = build_process_context(tp, backend="nccl", verbose=False)
         for fused in (True, False):
             cfg = TrainingConfig.from_yaml(os.path.join(root, "config", "test_tiny.yaml"))
@@ -113,19 +128,32 @@ def main():
             cfg.data.seq_len, cfg.data.micro_batch_size, cfg.data.dataset_path = 256, 2, "uniform"
             cfg.parallel.tp_size = tp
             cfg.parallel.sequence_parallel = sp
+            cfg.parallel.loss_parallel = lp
             cfg.parallel.param_dtype = "bfloat16"
             cfg.backend = "nccl"
             cfg.kernels.fused_comm = fused
             cfg.eval_interval = cfg.save_interval = 0
             cfg.log_interval = 10 ** 9
             tr = Trainer(cfg, ctx=ctx, gpu_type="b200")
-            losses = []
+            steps = []
             for _ in range(3):
                 wdw, _ = tr._next_window()
-                losses.append(train_step(tr.model, wdw, tr.optimizer, tr.scheduler, ctx, cfg).loss)
-            results[(tp, sp, fused)] = losses
-        lf, ln = results[(tp, sp, True)], results[(tp, sp, False)]
-        check(all(abs(p - q) < 2e-2 for p, q in zip(lf, ln)), f"tp={tp} sp={sp}: fused {lf} vs nccl {ln}")
+                m = train_step(tr.model, wdw, tr.optimizer, tr.scheduler, ctx, cfg)
+                steps.append((m.loss, m.grad_norm))
+            results[(tp, sp, lp, fused)] = steps
+            # every rank reports the same loss and norm
+            t = torch.tensor([v for st in steps for v in st], device=dev, dtype=torch.float64)
+            every = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(every, t)
+            check(all(torch.equal(every[0], e) for e in every), f"tp={tp} sp={sp} lp={lp} fused={fused}: ranks disagree")
+        sf, sn = results[(tp, sp, lp, True)], results[(tp, sp, lp, False)]
+        for i, ((lf, gf), (ln, gn)) in enumerate(zip(sf, sn)):
+            check(abs(lf - ln) < 1e-3 * (i + 1), f"tp={tp} sp={sp} lp={lp} step {i}: loss fused {lf} vs nccl {ln}")
+            check(abs(gf - gn) < 1e-2 * max(1.0, gn), f"tp={tp} sp={sp} lp={lp} step {i}: grad norm {gf} vs {gn}")
+    # the vocabulary-parallel loss equals the replicated-head loss on the same data
+    for fused in (True, False):
+        a, b = results[(world, False, True, fused)], results[(world, False, False, fused)]
+        check(abs(a[0][0] - b[0][0]) < 1e-3, f"loss_parallel first loss {a[0][0]} vs replicated head {b[0][0]}")
     torch.cuda.synchronize()
     check(native().device_error() == 0, "device error word set after training")
     if rank == 0:

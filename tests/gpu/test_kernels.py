@@ -3,6 +3,7 @@
 from __future__ import annotations
 
 import math
+import os
 
 import pytest
 import torch
@@ -119,6 +120,53 @@ def test_gemm_peer_allreduce_emulated_partner(M, N, K):
     assert _rel(out, ref) < 1e-2
     # rank 0 published its own tile to the partner's flag array
     assert int((heaps[1][flag_off:].view(torch.int32) == 7).sum()) > 0
+
+
+def _two_shot_owner_map(M: int, N: int, ranks: int) -> torch.Tensor:
+    """Owner rank of every (32-row group, output column) under the two-shot schedule:
+    the (tile, quadrant) unit f belongs to rank f % ranks (csrc/gemm.cu two_shot_owner)."""
+    BN = 256 if N > 128 else 128
+    pair = BN == 256 and M > 128 and os.environ.get("DTB_GEMM_PAIR", "1") != "0"
+    tile_m = 256 if pair else 128
+    mblocks, nblocks = -(-M // tile_m), -(-N // BN)
+    own = torch.empty(-(-M // 32) + 8, N, dtype=torch.int64)
+    for tile in range(mblocks * nblocks):
+        per_group = 16 * nblocks
+        g = tile // per_group
+        gm = min(16, mblocks - g * 16)
+        r = tile - g * per_group
+        mb, nb = g * 16 + r % gm, r // gm
+        for cta in range(2 if pair else 1):
+            ftile = 2 * tile + cta if pair else tile
+            slab = 2 * mb + cta if pair else mb
+            for q in range(4):
+                own[slab * 4 + q, nb * BN:(nb + 1) * BN] = (ftile * 4 + q) % ranks
+    return own[:-(-M // 32)].repeat_interleave(32, dim=0)[:M]
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 1024, 512), (200, 384, 256), (4096, 4096, 2048)])
+def test_gemm_peer_allreduce_two_shot_emulated_partner(M, N, K):
+    """Two-shot fused all-reduce, rank 0 of 2 with the partner emulated by memory: rank 0 sums the
+    units it owns (and writes the sum back to its staging) and copies the partner's units from the
+    partner's staging, where the emulated partner has already left its sum."""
+    a, b, r = _rand(M, K), _rand(N, K), _rand(M, N)
+    partner = _rand(M, N)
+    stage = M * N * 2
+    flag_off = (stage + 255) // 256 * 256
+    nflags = 2 * (M // 128 + 2) * (N // 128 + 2) * 4
+    heaps = [torch.zeros(flag_off + 3 * nflags * 4, device=DEV, dtype=torch.uint8) for _ in range(2)]
+    heaps[1][:stage].view(BF).copy_(partner.reshape(-1))
+    heaps[0][flag_off:].view(torch.int32).fill_(9)  # partner's partial flags and done flags
+    out = torch.empty(M, N, device=DEV, dtype=BF)
+    native().gemm_peer_ar(a, b, out, False, r, None, [h.data_ptr() for h in heaps], 0, 0, flag_off, 9, 1.0,
+                          two_shot=True)
+    mine = (a.float() @ b.float().t()).to(BF).float()
+    own = _two_shot_owner_map(M, N, 2).to(DEV)
+    ref = torch.where(own == 0, mine + partner.float() + r.float(), partner.float())
+    assert _rel(out, ref) < 1e-2
+    assert (own == 0).any() and (own == 1).any()
+    staged0 = heaps[0][:stage].view(BF).view(M, N)
+    assert torch.equal(staged0[own == 0], out[own == 0])  # the owner's sum, for the partner to copy
 
 
 @pytest.mark.parametrize("M,N,K", [(1024, 768, 512), (4096, 4096, 2048)])

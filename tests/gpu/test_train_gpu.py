@@ -1,4 +1,4 @@
-"""Bit-exact resume and activation-checkpointing equality on the GPU path (1 and 2 GPUs)."""
+"""Bit-exact resume and activation-checkpointing equality on the GPU path (1, 2 and 4 GPUs)."""
 
 import os
 import subprocess
@@ -15,11 +15,11 @@ if not torch.cuda.is_available():  # pragma: no cover
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-@pytest.mark.parametrize("n", [1, 2])
-def test_resume_and_checkpointing_are_bit_exact(n):
+@pytest.mark.parametrize("n,tp", [(1, 1), (2, 2), (4, 2)])
+def test_resume_and_checkpointing_are_bit_exact(n, tp):
     if torch.cuda.device_count() < n:
         pytest.skip(f"needs {n} GPUs")
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", DTB_PG_TIMEOUT_S="120")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", DTB_PG_TIMEOUT_S="120", DTB_TEST_TP=str(tp))
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
            "--master-addr", "127.0.0.1", "--master-port", str(29681 + n), os.path.join(HERE, "train_worker.py")]
     r = subprocess.run(["timeout", "-k", "30", "600"] + cmd, env=env, capture_output=True, text=True)

@@ -1,6 +1,7 @@
 """torchrun worker: bit-exact resume and activation checkpointing on the GPU path.
 
-Run by ``test_train_gpu.py`` with 1 rank (tp=1) or 2 ranks (tp=2).  A
+Run by ``test_train_gpu.py`` with 1 rank (tp=1), 2 ranks (tp=2) or 4 ranks
+(tp=2 x dp=2, the 2-D layout with ZeRO sharded checkpoints; ``DTB_TEST_TP``).  A
 continuous run and a save-at-step-3 / resume run must give identical losses
 and fp32 master weights, and a run with per-block activation checkpointing
 must match the run without it bit for bit.  Prints TRAIN_OK on success.
@@ -41,7 +42,7 @@ def steps(t, ctx, cfg, n):
 
 
 def main():
-    tp = int(os.environ["WORLD_SIZE"])
+    tp = int(os.environ.get("DTB_TEST_TP", os.environ["WORLD_SIZE"]))
     ctx = build_process_context(tp, backend="nccl", verbose=False)
     tmp = tempfile.mkdtemp() if ctx.rank == 0 else None
     box = [tmp]

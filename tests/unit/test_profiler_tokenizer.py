@@ -9,11 +9,14 @@ from build_your_own_distributed_training_b200.observability.profiler import is_c
 PEER_AR = "void dtb::gemm_tcgen05_kernel<256, 6, 1, 1, 6, 1>(CUtensorMap_st, CUtensorMap_st, dtb::GemmArgs)"
 SWIGLU = "void dtb::gemm_tcgen05_kernel<256, 6, 0, 0, 5, 1>(CUtensorMap_st, CUtensorMap_st, dtb::GemmArgs)"
 ACC = "void dtb::gemm_tcgen05_kernel<256, 6, 1, 1, 2, 1>(CUtensorMap_st, CUtensorMap_st, dtb::GemmArgs)"
+PEER_AR_BOOLS = "void dtb::gemm_tcgen05_kernel<256, 6, false, true, 6, true>(CUtensorMap_st, CUtensorMap_st, dtb::GemmArgs)"
+ROPE_BOOLS = "void dtb::gemm_tcgen05_kernel<256, 6, false, false, 4, true>(CUtensorMap_st, CUtensorMap_st, dtb::GemmArgs)"
 
 
 def test_peer_epilogue_gemm_is_fused_not_compute_or_comm():
     assert is_fused_comm_kernel(PEER_AR) and not is_comm_kernel(PEER_AR)
-    for name in (SWIGLU, ACC):
+    assert is_fused_comm_kernel(PEER_AR_BOOLS) and not is_fused_comm_kernel(ROPE_BOOLS)
+    for name in (SWIGLU, ACC, ROPE_BOOLS):
         assert not is_fused_comm_kernel(name) and not is_comm_kernel(name)
 
 
