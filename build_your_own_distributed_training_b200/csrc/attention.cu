@@ -1,5 +1,11 @@
 // Causal grouped-query flash attention, forward and backward (sm_100a).
 //
+// These mma.sync kernels cover every shape the tcgen05 kernels
+// (attention_tc.cu, attention_bwd_tc.cu: head_dim 64/128, seq_len % 128 == 0)
+// do not: head_dim 16, 32, 64 or 128 and any seq_len.  Rows past the end of
+// the sequence are zero-filled on load and never stored; padded query rows get
+// lse = +inf in the backward so their probabilities are exactly 0.
+//
 // Inputs come straight from the packed projection qkv[b*s, (nq + 2 nkv) * hd]
 // (q heads, then k heads, then v heads); query head h reads kv head
 // h / (nq / nkv), so nothing is repeated or transposed in memory.
@@ -33,6 +39,11 @@ constexpr float LOG2E = 1.4426950408889634f;
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
+// 16-byte copy that writes zeros instead when `valid` is false (source not read)
+__device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, bool valid) {
+  const int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(n) : "memory");
+}
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_wait() {
@@ -62,17 +73,20 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
 // ldmatrix conflict-free.
 template <int HD>
 __device__ __forceinline__ uint32_t swz(int row, int col) {  // byte offset of element (row, col)
-  const int chunk = (col >> 3) ^ (row & 7);
+  constexpr int CHR = HD / 8 < 8 ? HD / 8 : 8;              // 16-byte chunks a row's XOR may span
+  const int chunk = (col >> 3) ^ (row & (CHR - 1));
   return (uint32_t)(row * HD * 2 + chunk * 16 + (col & 7) * 2);
 }
 
+// rows [0, valid) come from g, rows [valid, R) are zero-filled
 template <int R, int HD, int NT>
-__device__ __forceinline__ void load_tile(uint8_t* s, const __nv_bfloat16* g, long ld) {
+__device__ __forceinline__ void load_tile(uint8_t* s, const __nv_bfloat16* g, long ld, int valid = R) {
   constexpr int CH = HD / 8;
 #pragma unroll
   for (int i = threadIdx.x; i < R * CH; i += NT) {
     const int r = i / CH, c = i % CH;
-    cp_async16(s + swz<HD>(r, c * 8), g + (long)r * ld + c * 8);
+    const bool ok = r < valid;
+    cp_async16_zfill(s + swz<HD>(r, c * 8), g + (ok ? (long)r * ld + c * 8 : 0), ok);
   }
 }
 
@@ -113,7 +127,7 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const __nv_bfloat16* __re
   uint8_t* sQ = sm;
   uint8_t* sK = sm + BM * HD * 2;             // [2][BN][HD]
   uint8_t* sV = sK + 2 * BN * HD * 2;         // [2][BN][HD]
-  const int nqb = S / BM;
+  const int nqb = (S + BM - 1) / BM;
   const int qb = nqb - 1 - blockIdx.x;  // heavy tiles first
   const int h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (nq / nkv);
@@ -125,9 +139,9 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const __nv_bfloat16* __re
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
 
-  load_tile<BM, HD, 128>(sQ, gq, ld);
-  load_tile<BN, HD, 128>(sK, gk, ld);
-  load_tile<BN, HD, 128>(sV, gv, ld);
+  load_tile<BM, HD, 128>(sQ, gq, ld, S - qb * BM);
+  load_tile<BN, HD, 128>(sK, gk, ld, S);
+  load_tile<BN, HD, 128>(sV, gv, ld, S);
   cp_commit();
 
   float o[HD / 8][4];
@@ -141,8 +155,8 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const __nv_bfloat16* __re
   for (int j = 0; j < nkb; ++j) {
     const int buf = j & 1;
     if (j + 1 < nkb) {
-      load_tile<BN, HD, 128>(sK + (buf ^ 1) * BN * HD * 2, gk + (long)(j + 1) * BN * ld, ld);
-      load_tile<BN, HD, 128>(sV + (buf ^ 1) * BN * HD * 2, gv + (long)(j + 1) * BN * ld, ld);
+      load_tile<BN, HD, 128>(sK + (buf ^ 1) * BN * HD * 2, gk + (long)(j + 1) * BN * ld, ld, S - (j + 1) * BN);
+      load_tile<BN, HD, 128>(sV + (buf ^ 1) * BN * HD * 2, gv + (long)(j + 1) * BN * ld, ld, S - (j + 1) * BN);
     }
     cp_commit();
     cp_wait<1>();
@@ -229,13 +243,13 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const __nv_bfloat16* __re
   __nv_bfloat16* o1 = o0 + 8 * ldo;
 #pragma unroll
   for (int n = 0; n < HD / 8; ++n) {
-    *reinterpret_cast<uint32_t*>(o0 + n * 8 + 2 * t) = pack_bf16x2(o[n][0] * inv0, o[n][1] * inv0);
-    *reinterpret_cast<uint32_t*>(o1 + n * 8 + 2 * t) = pack_bf16x2(o[n][2] * inv1, o[n][3] * inv1);
+    if (row0 < S) *reinterpret_cast<uint32_t*>(o0 + n * 8 + 2 * t) = pack_bf16x2(o[n][0] * inv0, o[n][1] * inv0);
+    if (row1 < S) *reinterpret_cast<uint32_t*>(o1 + n * 8 + 2 * t) = pack_bf16x2(o[n][2] * inv1, o[n][3] * inv1);
   }
   if (t == 0) {
     float* L = lse + ((long)b * nq + h) * S;
-    L[row0] = (m0 + log2f(l0)) / LOG2E;
-    L[row1] = (m1 + log2f(l1)) / LOG2E;
+    if (row0 < S) L[row0] = (m0 + log2f(l0)) / LOG2E;
+    if (row1 < S) L[row1] = (m1 + log2f(l1)) / LOG2E;
   }
 }
 
@@ -279,7 +293,7 @@ __global__ void __launch_bounds__(128) attn_bwd_dkdv_kernel(const __nv_bfloat16*
   uint8_t* sO = sQ + 2 * BQ * HD * 2;     // [2][BQ][HD]   (dO)
   float* sL = reinterpret_cast<float*>(sO + 2 * BQ * HD * 2);  // [2][BQ] lse*log2e
   float* sD = sL + 2 * BQ;                                     // [2][BQ]
-  const int nkb = S / BN;
+  const int nkb = (S + BN - 1) / BN;
   const int kb = nkb - 1 - blockIdx.x;  // tiles near the end see the fewest query tiles
   const int hk = blockIdx.y, b = blockIdx.z;
   const int grp = nq / nkv;
@@ -290,8 +304,8 @@ __global__ void __launch_bounds__(128) attn_bwd_dkdv_kernel(const __nv_bfloat16*
   const int g = lane >> 2, t = lane & 3;
   const int kv0 = kb * BN;
 
-  load_tile<BN, HD, 128>(sK, base + (long)kv0 * ld + (nq + hk) * HD, ld);
-  load_tile<BN, HD, 128>(sV, base + (long)kv0 * ld + (nq + nkv + hk) * HD, ld);
+  load_tile<BN, HD, 128>(sK, base + (long)kv0 * ld + (nq + hk) * HD, ld, S - kv0);
+  load_tile<BN, HD, 128>(sV, base + (long)kv0 * ld + (nq + nkv + hk) * HD, ld, S - kv0);
   cp_commit();
 
   float dk[HD / 8][4], dv[HD / 8][4];
@@ -301,17 +315,19 @@ __global__ void __launch_bounds__(128) attn_bwd_dkdv_kernel(const __nv_bfloat16*
     for (int e = 0; e < 4; ++e) dk[i][e] = dv[i][e] = 0.f;
 
   const int q_first = kv0 / BQ;
-  const int nqt = S / BQ - q_first;  // query tiles per head
+  const int nqt = (S + BQ - 1) / BQ - q_first;  // query tiles per head
   const int total = nqt * grp;
   auto issue = [&](int it, int buf) {
     const int hh = hk * grp + it / nqt;
     const int q0 = (q_first + it % nqt) * BQ;
-    load_tile<BQ, HD, 128>(sQ + buf * BQ * HD * 2, base + (long)q0 * ld + hh * HD, ld);
-    load_tile<BQ, HD, 128>(sO + buf * BQ * HD * 2, dO + ((long)b * S + q0) * ldo + hh * HD, ldo);
+    load_tile<BQ, HD, 128>(sQ + buf * BQ * HD * 2, base + (long)q0 * ld + hh * HD, ld, S - q0);
+    load_tile<BQ, HD, 128>(sO + buf * BQ * HD * 2, dO + ((long)b * S + q0) * ldo + hh * HD, ldo, S - q0);
     if (threadIdx.x < BQ) {
+      // padded query rows: lse = +inf makes their probabilities exactly 0
+      const bool in = q0 + (int)threadIdx.x < S;
       const long li = ((long)b * nq + hh) * S + q0 + threadIdx.x;
-      sL[buf * BQ + threadIdx.x] = lse[li] * LOG2E;
-      sD[buf * BQ + threadIdx.x] = Dv[li];
+      sL[buf * BQ + threadIdx.x] = in ? lse[li] * LOG2E : INFINITY;
+      sD[buf * BQ + threadIdx.x] = in ? Dv[li] : 0.f;
     }
   };
   issue(0, 0);
@@ -390,10 +406,14 @@ __global__ void __launch_bounds__(128) attn_bwd_dkdv_kernel(const __nv_bfloat16*
 #pragma unroll
   for (int n = 0; n < HD / 8; ++n) {
     const int c = n * 8 + 2 * t;
-    *reinterpret_cast<uint32_t*>(gk0 + c) = pack_bf16x2(dk[n][0] * scale, dk[n][1] * scale);
-    *reinterpret_cast<uint32_t*>(gk0 + 8 * ldd + c) = pack_bf16x2(dk[n][2] * scale, dk[n][3] * scale);
-    *reinterpret_cast<uint32_t*>(gv0 + c) = pack_bf16x2(dv[n][0], dv[n][1]);
-    *reinterpret_cast<uint32_t*>(gv0 + 8 * ldd + c) = pack_bf16x2(dv[n][2], dv[n][3]);
+    if (krow0 < S) {
+      *reinterpret_cast<uint32_t*>(gk0 + c) = pack_bf16x2(dk[n][0] * scale, dk[n][1] * scale);
+      *reinterpret_cast<uint32_t*>(gv0 + c) = pack_bf16x2(dv[n][0], dv[n][1]);
+    }
+    if (krow0 + 8 < S) {
+      *reinterpret_cast<uint32_t*>(gk0 + 8 * ldd + c) = pack_bf16x2(dk[n][2] * scale, dk[n][3] * scale);
+      *reinterpret_cast<uint32_t*>(gv0 + 8 * ldd + c) = pack_bf16x2(dv[n][2], dv[n][3]);
+    }
   }
 }
 
@@ -409,7 +429,7 @@ __global__ void __launch_bounds__(128) attn_bwd_dq_kernel(const __nv_bfloat16* _
   uint8_t* sO = sQ + BM * HD * 2;       // [BM][HD]
   uint8_t* sK = sO + BM * HD * 2;       // [2][BN][HD]
   uint8_t* sV = sK + 2 * BN * HD * 2;   // [2][BN][HD]
-  const int nqb = S / BM;
+  const int nqb = (S + BM - 1) / BM;
   const int qbk = nqb - 1 - blockIdx.x;
   const int h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (nq / nkv);
@@ -421,25 +441,26 @@ __global__ void __launch_bounds__(128) attn_bwd_dq_kernel(const __nv_bfloat16* _
   const int q0 = qbk * BM;
   const __nv_bfloat16* gk = base + (long)(nq + hk) * HD;
   const __nv_bfloat16* gv = base + (long)(nq + nkv + hk) * HD;
-  load_tile<BM, HD, 128>(sQ, base + (long)q0 * ld + h * HD, ld);
-  load_tile<BM, HD, 128>(sO, dO + ((long)b * S + q0) * ldo + h * HD, ldo);
-  load_tile<BN, HD, 128>(sK, gk, ld);
-  load_tile<BN, HD, 128>(sV, gv, ld);
+  load_tile<BM, HD, 128>(sQ, base + (long)q0 * ld + h * HD, ld, S - q0);
+  load_tile<BM, HD, 128>(sO, dO + ((long)b * S + q0) * ldo + h * HD, ldo, S - q0);
+  load_tile<BN, HD, 128>(sK, gk, ld, S);
+  load_tile<BN, HD, 128>(sV, gv, ld, S);
   cp_commit();
   const int row0 = q0 + warp * 16 + g, row1 = row0 + 8;
   const long li = ((long)b * nq + h) * S;
-  const float L0 = lse[li + row0] * LOG2E, L1 = lse[li + row1] * LOG2E;
-  const float D0 = Dv[li + row0], D1 = Dv[li + row1];
+  const float L0 = row0 < S ? lse[li + row0] * LOG2E : INFINITY;
+  const float L1 = row1 < S ? lse[li + row1] * LOG2E : INFINITY;
+  const float D0 = row0 < S ? Dv[li + row0] : 0.f, D1 = row1 < S ? Dv[li + row1] : 0.f;
   float dq[HD / 8][4];
 #pragma unroll
   for (int i = 0; i < HD / 8; ++i) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.f;
   uint32_t qf[HD / 16][4], of[HD / 16][4];
-  const int nkt = (q0 + BM) / BN;
+  const int nkt = min((q0 + BM) / BN, (S + BN - 1) / BN);
   for (int j = 0; j < nkt; ++j) {
     const int buf = j & 1;
     if (j + 1 < nkt) {
-      load_tile<BN, HD, 128>(sK + (buf ^ 1) * BN * HD * 2, gk + (long)(j + 1) * BN * ld, ld);
-      load_tile<BN, HD, 128>(sV + (buf ^ 1) * BN * HD * 2, gv + (long)(j + 1) * BN * ld, ld);
+      load_tile<BN, HD, 128>(sK + (buf ^ 1) * BN * HD * 2, gk + (long)(j + 1) * BN * ld, ld, S - (j + 1) * BN);
+      load_tile<BN, HD, 128>(sV + (buf ^ 1) * BN * HD * 2, gv + (long)(j + 1) * BN * ld, ld, S - (j + 1) * BN);
     }
     cp_commit();
     cp_wait<1>();
@@ -502,8 +523,8 @@ __global__ void __launch_bounds__(128) attn_bwd_dq_kernel(const __nv_bfloat16* _
 #pragma unroll
   for (int n = 0; n < HD / 8; ++n) {
     const int c = n * 8 + 2 * t;
-    *reinterpret_cast<uint32_t*>(g0 + c) = pack_bf16x2(dq[n][0] * scale, dq[n][1] * scale);
-    *reinterpret_cast<uint32_t*>(g0 + 8 * ld + c) = pack_bf16x2(dq[n][2] * scale, dq[n][3] * scale);
+    if (row0 < S) *reinterpret_cast<uint32_t*>(g0 + c) = pack_bf16x2(dq[n][0] * scale, dq[n][1] * scale);
+    if (row1 < S) *reinterpret_cast<uint32_t*>(g0 + 8 * ld + c) = pack_bf16x2(dq[n][2] * scale, dq[n][3] * scale);
   }
 }
 
@@ -516,7 +537,7 @@ void fwd_launch(const __nv_bfloat16* qkv, __nv_bfloat16* o, float* lse, int B, i
     DTB_CUDA(cudaFuncSetAttribute(attn_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     cfg = true;
   }
-  dim3 grid(S / 64, nq, B);
+  dim3 grid((S + 63) / 64, nq, B);
   attn_fwd_kernel<HD><<<grid, 128, smem, st>>>(qkv, o, lse, S, nq, nkv, scale * LOG2E);
 }
 
@@ -538,10 +559,10 @@ void bwd_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* o, const __nv_bfl
     DTB_CUDA(cudaFuncSetAttribute(attn_bwd_dq_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q));
     cfg = true;
   }
-  attn_bwd_dkdv_kernel<HD><<<dim3(S / 64, nkv, B), 128, smem_kv, st>>>(qkv, dO, lse, Dv, dqkv, S, nq, nkv, scale,
-                                                                        scale * LOG2E);
-  attn_bwd_dq_kernel<HD><<<dim3(S / 64, nq, B), 128, smem_q, st>>>(qkv, dO, lse, Dv, dqkv, S, nq, nkv, scale,
-                                                                    scale * LOG2E);
+  attn_bwd_dkdv_kernel<HD><<<dim3((S + 63) / 64, nkv, B), 128, smem_kv, st>>>(qkv, dO, lse, Dv, dqkv, S, nq, nkv,
+                                                                               scale, scale * LOG2E);
+  attn_bwd_dq_kernel<HD><<<dim3((S + 63) / 64, nq, B), 128, smem_q, st>>>(qkv, dO, lse, Dv, dqkv, S, nq, nkv, scale,
+                                                                           scale * LOG2E);
 }
 
 }  // namespace attn
@@ -551,8 +572,8 @@ using namespace dtb;
 
 static void attn_check(const torch::Tensor& qkv, int64_t B, int64_t S, int64_t nq, int64_t nkv, int64_t hd) {
   TORCH_CHECK(qkv.is_cuda() && qkv.scalar_type() == at::kBFloat16 && qkv.is_contiguous(), "attention: bf16 packed qkv");
-  TORCH_CHECK(hd == 64 || hd == 128, "attention kernel supports head_dim 64 and 128");
-  TORCH_CHECK(S % 64 == 0, "attention kernel needs seq_len % 64 == 0");
+  TORCH_CHECK(hd == 16 || hd == 32 || hd == 64 || hd == 128, "attention kernels support head_dim 16, 32, 64 and 128");
+  TORCH_CHECK(S >= 1 && B >= 1, "attention: empty batch or sequence");
   TORCH_CHECK(nq % nkv == 0, "nq must be a multiple of nkv");
   TORCH_CHECK(qkv.size(0) == B * S && qkv.size(1) == (nq + 2 * nkv) * hd, "attention: qkv shape");
 }
@@ -572,7 +593,9 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t B, int64_t S, int
   auto q = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
   auto op = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
   if (hd == 128) attn::fwd_launch<128>(q, op, lse.data_ptr<float>(), B, S, nq, nkv, (float)scale, st);
-  else attn::fwd_launch<64>(q, op, lse.data_ptr<float>(), B, S, nq, nkv, (float)scale, st);
+  else if (hd == 64) attn::fwd_launch<64>(q, op, lse.data_ptr<float>(), B, S, nq, nkv, (float)scale, st);
+  else if (hd == 32) attn::fwd_launch<32>(q, op, lse.data_ptr<float>(), B, S, nq, nkv, (float)scale, st);
+  else attn::fwd_launch<16>(q, op, lse.data_ptr<float>(), B, S, nq, nkv, (float)scale, st);
   DTB_LAUNCH_CHECK();
   return {o, lse};
 }
@@ -591,17 +614,21 @@ torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qkv, torch::Tensor o, tor
   auto cast = [](const torch::Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr()); };
   auto dq = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
   if (hd == 128) attn::bwd_pre_launch<128>(cast(o), cast(dO), Dv.data_ptr<float>(), B, S, nq, st);
-  else attn::bwd_pre_launch<64>(cast(o), cast(dO), Dv.data_ptr<float>(), B, S, nq, st);
+  else if (hd == 64) attn::bwd_pre_launch<64>(cast(o), cast(dO), Dv.data_ptr<float>(), B, S, nq, st);
+  else if (hd == 32) attn::bwd_pre_launch<32>(cast(o), cast(dO), Dv.data_ptr<float>(), B, S, nq, st);
+  else attn::bwd_pre_launch<16>(cast(o), cast(dO), Dv.data_ptr<float>(), B, S, nq, st);
   DTB_LAUNCH_CHECK();
   // tcgen05/TMEM kernels (attention_bwd_tc.cu) unless the sequence is not a multiple of 128
   if (!legacy && attn_bwd_tc(dO, qkv, lse.data_ptr<float>(), Dv.data_ptr<float>(), dqkv, B, S, nq, nkv, hd, scale))
     return dqkv;
-  if (hd == 128)
-    attn::bwd_launch<128>(cast(qkv), cast(o), cast(dO), lse.data_ptr<float>(), Dv.data_ptr<float>(), dq, B, S, nq, nkv,
-                          (float)scale, st);
-  else
-    attn::bwd_launch<64>(cast(qkv), cast(o), cast(dO), lse.data_ptr<float>(), Dv.data_ptr<float>(), dq, B, S, nq, nkv,
-                         (float)scale, st);
+#define DTB_ATTN_BWD(HDV)                                                                                            \
+  attn::bwd_launch<HDV>(cast(qkv), cast(o), cast(dO), lse.data_ptr<float>(), Dv.data_ptr<float>(), dq, B, S, nq, nkv, \
+                        (float)scale, st)
+  if (hd == 128) DTB_ATTN_BWD(128);
+  else if (hd == 64) DTB_ATTN_BWD(64);
+  else if (hd == 32) DTB_ATTN_BWD(32);
+  else DTB_ATTN_BWD(16);
+#undef DTB_ATTN_BWD
   DTB_LAUNCH_CHECK();
   return dqkv;
 }

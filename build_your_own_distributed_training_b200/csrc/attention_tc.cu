@@ -1,7 +1,7 @@
 // Causal GQA flash-attention forward on the 5th-generation tensor cores
 // (tcgen05 + TMEM + TMA), sm_100a.
 //
-// One CTA per (128-row query tile, head, batch); 6 warps:
+// One CTA per (128-row query tile, head, batch); 10 warps:
 //   warp 0     TMA producer: the Q tile once, then K and V tiles (128 keys)
 //              into 2-deep rings, straight from the packed qkv projection;
 //   warp 1     owns TMEM (512 columns: two 128-column S buffers + the O
@@ -9,15 +9,24 @@
 //                S_j = Q K_j^T   (M=128, N=128, K=hd; both operands K-major)
 //                O  += P_j V_j   (M=128, N=hd,  K=128; V is MN-major)
 //              S_{j+1} is computed while the softmax warps work on S_j;
-//   warps 2-5  softmax: thread t owns query row t (TMEM lane t), reads its S
-//              row with four tcgen05.ld and one wait, applies the causal mask
-//              (diagonal tile only) and the online softmax in exp2 form with
-//              the scale folded into one FFMA, writes P_j in bf16 to one of
-//              two shared-memory buffers in the 128-byte-swizzled K-major
-//              layout the MMA reads, and finally normalises O and writes it
-//              out with the log-sum-exp.  With two P buffers the softmax of
-//              tile j only waits for the PV product of tile j-2 (normally long
-//              done), so it runs concurrently with PV_{j-1} and S_{j+1}.
+//   warps 2-9  softmax, two threads per query row: warps w and w+4 read the
+//              same TMEM lanes (32*(w%4)..+31 = query rows), warp w columns
+//              [0, 64) of S and warp w+4 columns [64, 128) (and the matching
+//              halves of O).  Each thread reads its 64 scores with two
+//              tcgen05.ld and one wait, applies the causal mask (diagonal tile
+//              only), takes its half-row maximum and swaps it with its partner
+//              through shared memory (a 64-thread named barrier per row
+//              quarter), then runs the online softmax in exp2 form with the
+//              scale folded into one FFMA.  One exponential in four is
+//              evaluated on the FMA pipes (exp2_fma below) instead of the
+//              special-function unit, whose rate (16 per clock per SM) bounds
+//              this stage.  P_j goes in bf16 to one of two shared-memory
+//              buffers in the 128-byte-swizzled K-major layout the MMA reads
+//              (each thread writes one 64-column atom of its row); with two P
+//              buffers the softmax of tile j only waits for the PV product of
+//              tile j-2, so it runs concurrently with PV_{j-1} and S_{j+1}.
+//              At the end the partners add their partial row sums, normalise
+//              their halves of O and write them with the log-sum-exp.
 //
 // O is rescaled only when a row's running maximum grows by more than 8 (in
 // log2 units): until then P = exp2(s - m_stale) <= 2^8, which fp32 and bf16
@@ -38,6 +47,30 @@ namespace fa {
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr int BM = 128, BN = 128;
 constexpr float RESCALE_THRESHOLD = 8.f;
+constexpr int SOFTMAX_THREADS = 256;   // warps 2-9
+constexpr int NTHREADS = 64 + SOFTMAX_THREADS;
+
+// 2^x on the FMA/ALU pipes, for x <= RESCALE_THRESHOLD (masked scores are
+// -inf).  Range reduction x = n + f with n = round(x) taken from the mantissa
+// of x + 1.5 * 2^23 (f in [-1/2, 1/2]), 2^f by the degree-3 polynomial that
+// interpolates it at the four Chebyshev nodes of [-1/2, 1/2] (coefficients
+// computed for this kernel; max relative error 1.0e-4, below the 2^-9 of the
+// bf16 P it feeds), and 2^n added to the result's exponent field.  Inputs
+// below -125 are clamped there, which gives a value below 2^-124 (the sums
+// and bf16 P treat it as 0).
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -125.f);
+  const float shifter = 12582912.f;  // 1.5 * 2^23
+  const float t = x + shifter;
+  const float n = t - shifter;       // round(x)
+  const float f = x - n;
+  float p = fmaf(0.05583828f, f, 0.24263948f);
+  p = fmaf(p, f, 0.69313675f);
+  p = fmaf(p, f, 0.99992454f);
+  const int e = __float_as_int(t) - __float_as_int(shifter);  // n as an integer
+  return __int_as_float(__float_as_int(p) + (e << 23));
+}
+
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
   asm volatile(
@@ -68,9 +101,11 @@ struct Smem {
   static constexpr int K_OFF = Q_OFF + Q_BYTES;         // 2 stages
   static constexpr int V_OFF = K_OFF + 2 * K_BYTES;     // 2 stages
   static constexpr int P_OFF = V_OFF + 2 * V_BYTES;   // 2 buffers
-  static constexpr int BAR_OFF = P_OFF + 2 * P_BYTES;
-  static constexpr int N_BARS = 18;
+  static constexpr int X_OFF = P_OFF + 2 * P_BYTES;     // [2 halves][128 rows] fp32 partner exchange
+  static constexpr int BAR_OFF = X_OFF + 2 * BM * 4;
+  static constexpr int N_BARS = 22;
   static constexpr int TOTAL = BAR_OFF + N_BARS * 8 + 16 + 1024;
+  static_assert(TOTAL <= 232448, "shared memory per CTA");
 };
 
 struct FwdArgs {
@@ -82,7 +117,7 @@ struct FwdArgs {
 };
 
 template <int HD>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(NTHREADS, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qk, const __grid_constant__ CUtensorMap tm_v,
                        const FwdArgs a) {
   using L = Smem<HD>;
@@ -98,6 +133,7 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* o_done = bars + 11;    // [2]: PV_j (read P buffer j & 1) finished
   uint64_t* v_full = bars + 13;    // [2]
   uint64_t* v_empty = bars + 15;   // [2]
+  uint64_t* x_bar = bars + 17;     // [4]: the two softmax threads of each row quarter (64 arrivals)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + L::N_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -117,10 +153,11 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&s_empty[i], SOFTMAX_THREADS);
+      mbar_init(&p_full[i], SOFTMAX_THREADS);
       mbar_init(&o_done[i], 1);
     }
+    for (int i = 0; i < 4; ++i) mbar_init(&x_bar[i], 64);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_qk);
@@ -230,10 +267,22 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // ------------------------------------------------------------ softmax warps
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;        // 0: columns [0, 64), 1: [64, 128)
     const int r = quad * 32 + lane;          // row within the tile == TMEM lane
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    float m_used = -INFINITY, l = 0.f;       // running max (log2 units) and sum
+    const int c0 = half * 64;                // first S column of this thread
+    float* xch = reinterpret_cast<float*>(sm + L::X_OFF);
+    float m_used = -INFINITY, l = 0.f;       // running max (log2 units) and this half's sum
     bool ok = true;
+    // rendezvous of the two threads of a row (bounded: a partner that left on an
+    // error makes this time out instead of hanging)
+    uint32_t xphase = 0;
+    auto xsync = [&]() -> bool {
+      mbar_arrive(&x_bar[quad]);
+      const bool r2 = mbar_wait(&x_bar[quad], xphase, a.err);
+      xphase ^= 1;
+      return r2;
+    };
     for (int j = 0; j < nkb; ++j) {
       const int st = j & 1;
       if (*abort_flag || !mbar_wait(&s_full[st], (j >> 1) & 1, a.err)) {
@@ -241,31 +290,43 @@ __global__ void __launch_bounds__(192, 1)
         break;
       }
       tc_fence_after();
-      uint32_t sr[4][32];
+      uint32_t sr[2][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32_async(t_s[st] + lane_off + c * 32, sr[c]);
+      for (int c = 0; c < 2; ++c) tmem_ld32_async(t_s[st] + lane_off + c0 + c * 32, sr[c]);
       tmem_wait_ld();
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_regs(sr[c]);
+      for (int c = 0; c < 2; ++c) tmem_regs(sr[c]);
       tc_fence_before();
       mbar_arrive(&s_empty[st]);  // S buffer free for S_{j+2}
-      float s[BN];
+      float sv[64];
 #pragma unroll
-      for (int c = 0; c < BN; ++c) s[c] = __uint_as_float(sr[c >> 5][c & 31]);
+      for (int c = 0; c < 64; ++c) sv[c] = __uint_as_float(sr[c >> 5][c & 31]);
       if (j == qb) {
         // diagonal tile: key column c is visible to query row r iff c <= r
 #pragma unroll
-        for (int c = 0; c < BN; ++c)
-          if (c > r) s[c] = -INFINITY;
+        for (int c = 0; c < 64; ++c)
+          if (c0 + c > r) sv[c] = -INFINITY;
       }
-      // row max of the raw scores, four independent chains
-      float mx4[4] = {s[0], s[1], s[2], s[3]};
+      float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};
 #pragma unroll
-      for (int c = 4; c < BN; c += 4) {
+      for (int c = 4; c < 64; c += 4) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) mx4[i] = fmaxf(mx4[i], s[c + i]);
+        for (int i = 0; i < 4; ++i) mx4[i] = fmaxf(mx4[i], sv[c + i]);
       }
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
+      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      // swap half-row maxima with the partner (same rows, other columns)
+      xch[half * BM + r] = mx;
+      if (!xsync()) {
+        ok = false;
+        *abort_flag = 1;
+        break;
+      }
+      mx = fmaxf(mx, xch[(half ^ 1) * BM + r]) * a.scale_log2;
+      if (!xsync()) {  // both read before the next write
+        ok = false;
+        *abort_flag = 1;
+        break;
+      }
       float alpha = 1.f;
       bool rescale = false;
       if (mx > m_used + RESCALE_THRESHOLD) {
@@ -273,56 +334,61 @@ __global__ void __launch_bounds__(192, 1)
         rescale = (m_used != -INFINITY);
         m_used = mx;
       }
-      // p = 2^(s * scale*log2e - m): one FFMA and one ex2 per element
+      // p = 2^(s * scale*log2e - m): one FFMA and one exponential per element,
+      // every fourth pair of columns on the FMA pipes
       const float neg_m = -m_used;
       float rs4[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[BN / 2];
+      uint32_t pk[32];
 #pragma unroll
-      for (int c = 0; c < BN; c += 2) {
-        const float p0 = ex2_approx(fmaf(s[c], a.scale_log2, neg_m));
-        const float p1 = ex2_approx(fmaf(s[c + 1], a.scale_log2, neg_m));
+      for (int c = 0; c < 64; c += 2) {
+        const float x0 = fmaf(sv[c], a.scale_log2, neg_m), x1 = fmaf(sv[c + 1], a.scale_log2, neg_m);
+        float p0, p1;
+        if ((c & 6) == 6) {
+          p0 = exp2_fma(x0);
+          p1 = exp2_fma(x1);
+        } else {
+          p0 = ex2_approx(x0);
+          p1 = ex2_approx(x1);
+        }
         rs4[(c >> 1) & 3] += p0 + p1;
         pk[c / 2] = pack_bf16x2(p0, p1);
       }
       l = l * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
       if (__any_sync(0xffffffffu, rescale)) {
-        // O holds PV_0..PV_{j-1}: wait for the last of them, then scale it
+        // O holds PV_0..PV_{j-1}: wait for the last of them, then scale this half
         if (j > 0) {
-          if (!mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, a.err)) {
-            ok = false;
-            break;
-          }
+          if (!mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, a.err)) ok = false;
           tc_fence_after();
         }
-        const float f = rescale ? alpha : 1.f;
+        if (ok) {
+          const float f = rescale ? alpha : 1.f;
 #pragma unroll 1
-        for (int c = 0; c < HD; c += 32) {
-          float o[32];
-          tmem_ld32(t_o + lane_off + c, o);
+          for (int c = half * (HD / 2); c < (half + 1) * (HD / 2); c += 32) {
+            float o[32];
+            tmem_ld32(t_o + lane_off + c, o);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= f;
-          tmem_st32(t_o + lane_off + c, o);
+            for (int i = 0; i < 32; ++i) o[i] *= f;
+            tmem_st32(t_o + lane_off + c, o);
+          }
+          tmem_st_wait();
         }
-        tmem_st_wait();
       }
       // P buffer j & 1 was last read by PV_{j-2}
-      if (j > 1) {
-        if (!mbar_wait(&o_done[j & 1], ((j - 2) >> 1) & 1, a.err)) {
-          ok = false;
-          break;
-        }
+      if (ok && j > 1 && !mbar_wait(&o_done[j & 1], ((j - 2) >> 1) & 1, a.err)) ok = false;
+      if (!ok) {
+        *abort_flag = 1;
+        break;
       }
-      // P row r -> two 64-column atoms, 16-byte chunks XOR-swizzled by (r % 8)
-      uint8_t* P = sm + L::P_OFF + (j & 1) * L::P_BYTES;
+      // this half of P row r -> its 64-column atom, 16-byte chunks XOR-swizzled by (r % 8)
+      uint8_t* P = sm + L::P_OFF + (j & 1) * L::P_BYTES + half * 16384 + r * 128;
 #pragma unroll
-      for (int ch = 0; ch < BN / 8; ++ch) {
-        const int atom = ch >> 3, cc = ch & 7;
+      for (int cc = 0; cc < 8; ++cc) {
         uint4 v;
-        v.x = pk[ch * 4 + 0];
-        v.y = pk[ch * 4 + 1];
-        v.z = pk[ch * 4 + 2];
-        v.w = pk[ch * 4 + 3];
-        *reinterpret_cast<uint4*>(P + atom * 16384 + r * 128 + ((cc ^ (r & 7)) << 4)) = v;
+        v.x = pk[cc * 4 + 0];
+        v.y = pk[cc * 4 + 1];
+        v.z = pk[cc * 4 + 2];
+        v.w = pk[cc * 4 + 3];
+        *reinterpret_cast<uint4*>(P + ((cc ^ (r & 7)) << 4)) = v;
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -330,11 +396,15 @@ __global__ void __launch_bounds__(192, 1)
     }
     if (ok && mbar_wait(&o_done[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1, a.err)) {
       tc_fence_after();
-      const float inv = 1.f / l;
+      // row sum = half 0 + half 1, the same order in both partners
+      xch[half * BM + r] = l;
+      if (!xsync()) *abort_flag = 1;
+      const float lt = xch[r] + xch[BM + r];
+      const float inv = 1.f / lt;
       const long orow = (long)row0 + qb * BM + r;
       __nv_bfloat16* op = a.out + orow * (long)a.nq * HD + h * HD;
 #pragma unroll 1
-      for (int c = 0; c < HD; c += 32) {
+      for (int c = half * (HD / 2); c < (half + 1) * (HD / 2); c += 32) {
         float o[32];
         tmem_ld32(t_o + lane_off + c, o);
 #pragma unroll
@@ -347,7 +417,7 @@ __global__ void __launch_bounds__(192, 1)
           *reinterpret_cast<uint4*>(op + c + i) = w;
         }
       }
-      a.lse[((long)b * a.nq + h) * a.S + qb * BM + r] = (m_used + log2f(l)) / LOG2E;
+      if (half == 0) a.lse[((long)b * a.nq + h) * a.S + qb * BM + r] = (m_used + log2f(lt)) / LOG2E;
     } else {
       *abort_flag = 1;
     }
@@ -402,7 +472,8 @@ void fwd_tc_launch(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& ls
   }
   FwdArgs args{reinterpret_cast<__nv_bfloat16*>(o.data_ptr()), lse.data_ptr<float>(), S, nq, nkv, scale * LOG2E,
                dtb_error_word()};
-  attn_fwd_tc_kernel<HD><<<dim3(S / BM, nq, B), 192, L::TOTAL, at::cuda::getCurrentCUDAStream()>>>(tqk, tv, args);
+  attn_fwd_tc_kernel<HD><<<dim3(S / BM, nq, B), NTHREADS, L::TOTAL, at::cuda::getCurrentCUDAStream()>>>(tqk, tv,
+                                                                                                        args);
   DTB_LAUNCH_CHECK();
 }
 

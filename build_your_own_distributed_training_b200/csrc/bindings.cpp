@@ -34,6 +34,8 @@ int64_t ipc_open(torch::Tensor handle);
 void ipc_close(int64_t ptr);
 void peer_barrier(std::vector<int64_t> bases, int64_t flag_off, int64_t rank, int64_t epoch, double timeout_s);
 void peer_all_gather(std::vector<int64_t> bases, int64_t src_off, int64_t shard_bytes, torch::Tensor out);
+void peer_all_gather_ce(std::vector<int64_t> bases, int64_t src_off, int64_t shard_bytes, torch::Tensor out,
+                        int64_t src_stride, int64_t skip_rank);
 int64_t reduce_scatter_blocks(int64_t n);
 void peer_reduce_scatter(std::vector<int64_t> bases, int64_t grad_off, int64_t rank, double scale, torch::Tensor out,
                          c10::optional<torch::Tensor> part, int64_t split, double rep_w);
@@ -84,6 +86,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &ipc_close);
   m.def("peer_barrier", &peer_barrier);
   m.def("peer_all_gather", &peer_all_gather);
+  m.def("peer_all_gather_ce", &peer_all_gather_ce, "all-gather with one copy-engine memcpy per rank",
+        py::arg("bases"), py::arg("src_off"), py::arg("shard_bytes"), py::arg("out"), py::arg("src_stride") = 0,
+        py::arg("skip_rank") = -1);
   m.def("peer_reduce_scatter", &peer_reduce_scatter, py::arg("bases"), py::arg("grad_off"), py::arg("rank"),
         py::arg("scale"), py::arg("out"), py::arg("part") = py::none(), py::arg("split") = 0, py::arg("rep_w") = 1.0);
   m.def("reduce_scatter_blocks", &reduce_scatter_blocks);

@@ -187,6 +187,19 @@ static int blocks_for(long work_items, int nt) {
   return (int)std::max<long>(1, std::min<long>(b, 8L * device_sm_count()));
 }
 
+// The gradient reduce-scatter overlaps the backward GEMMs on a side stream:
+// DTB_RS_CTAS caps its grid (default 2 per SM) so it leaves the SMs' issue
+// slots mostly to the GEMM that shares them.
+static int rs_blocks_for(long work_items, int nt) {
+  static long cap = -1;
+  if (cap < 0) {
+    const char* e = getenv("DTB_RS_CTAS");
+    cap = (e != nullptr && atol(e) > 0) ? atol(e) : 2L * device_sm_count();
+  }
+  long b = (work_items + nt - 1) / nt;
+  return (int)std::max<long>(1, std::min<long>(b, cap));
+}
+
 }  // namespace comm
 }  // namespace dtb
 
@@ -242,11 +255,32 @@ void peer_all_gather(std::vector<int64_t> bases, int64_t src_off, int64_t shard_
   DTB_LAUNCH_CHECK();
 }
 
+// All-gather on the copy engines: one cudaMemcpyAsync per rank from its heap
+// (peer memory through the IPC mapping) into this rank's output, on the
+// current stream.  No SM runs it, so a gather overlapped with GEMMs takes no
+// issue slots or registers from them.  Valid when every source shard is final
+// before the stream reaches the copies (ZeRO parameter shards: written by the
+// optimizer step, followed by a device barrier).
+// Rank p's piece is read at bases[p] + src_off + p * src_stride (src_stride 0:
+// every rank's piece at the same offset); skip_rank's piece is not copied (it
+// is already in place when `out` is that rank's own heap buffer).
+void peer_all_gather_ce(std::vector<int64_t> bases, int64_t src_off, int64_t shard_bytes, torch::Tensor out,
+                        int64_t src_stride, int64_t skip_rank) {
+  DTB_CHECK(out.numel() * out.element_size() >= shard_bytes * (long)bases.size(), "all-gather output too small");
+  auto* dst = reinterpret_cast<uint8_t*>(out.data_ptr());
+  for (size_t p = 0; p < bases.size(); ++p) {
+    if ((int64_t)p == skip_rank) continue;
+    DTB_CUDA(cudaMemcpyAsync(dst + p * shard_bytes,
+                             reinterpret_cast<const uint8_t*>(bases[p]) + src_off + (long)p * src_stride, shard_bytes,
+                             cudaMemcpyDeviceToDevice, cs()));
+  }
+}
+
 // Reduce-scatter (mean over the group) of an fp32 gradient buffer.  `part`
 // (optional, fp32, at least reduce_scatter_blocks(n) entries) receives the
 // per-block weighted sums of squares of the result (see the kernel); entries
 // past the blocks used are left untouched.
-int64_t reduce_scatter_blocks(int64_t n) { return blocks_for(n / 4, 256); }
+int64_t reduce_scatter_blocks(int64_t n) { return rs_blocks_for(n / 4, 256); }
 
 void peer_reduce_scatter(std::vector<int64_t> bases, int64_t grad_off, int64_t rank, double scale, torch::Tensor out,
                          c10::optional<torch::Tensor> part, int64_t split, double rep_w) {
@@ -254,7 +288,7 @@ void peer_reduce_scatter(std::vector<int64_t> bases, int64_t grad_off, int64_t r
   const long n = out.numel();
   DTB_CHECK(n % 4 == 0 && grad_off % 16 == 0, "reduce-scatter needs 16-byte aligned shards");
   auto peers = make_peers(bases);
-  const int nb = blocks_for(n / 4, 256);
+  const int nb = rs_blocks_for(n / 4, 256);
   float* pp = nullptr;
   if (part.has_value()) {
     DTB_CHECK(part->scalar_type() == at::kFloat && part->is_contiguous() && part->numel() >= nb,

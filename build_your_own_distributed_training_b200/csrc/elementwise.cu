@@ -457,6 +457,50 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ sorted_tok, con
   }
 }
 
+// Stable sort of the token ids for the embedding backward, in one CTA: key =
+// (id << shift) | position, so keys are unique and any correct sort is stable;
+// bitonic network over a power-of-two padded shared-memory array (pads are
+// 0xFFFFFFFF and sort last).  Ids outside [0, V) get the key of bucket V,
+// which embedding_bwd_kernel skips.  Writes the sorted ids and their positions.
+__global__ void __launch_bounds__(1024) sort_tokens_kernel(const int64_t* __restrict__ tok, int M, int V, int shift,
+                                                           int npow2, int64_t* __restrict__ sorted_tok,
+                                                           int64_t* __restrict__ order) {
+  extern __shared__ uint32_t keys[];
+  for (int i = threadIdx.x; i < npow2; i += blockDim.x) {
+    uint32_t k = 0xFFFFFFFFu;
+    if (i < M) {
+      const int64_t t = tok[i];
+      const uint32_t b = (t < 0 || t >= V) ? (uint32_t)V : (uint32_t)t;
+      k = (b << shift) | (uint32_t)i;
+    }
+    keys[i] = k;
+  }
+  __syncthreads();
+  for (int k = 2; k <= npow2; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < npow2; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const uint32_t a = keys[i], b = keys[ixj];
+          const bool ascending = (i & k) == 0;
+          if ((a > b) == ascending) {
+            keys[i] = b;
+            keys[ixj] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  const uint32_t mask = (1u << shift) - 1u;
+  for (int i = threadIdx.x; i < M; i += blockDim.x) {
+    const uint32_t k = keys[i];
+    const uint32_t b = k >> shift;
+    sorted_tok[i] = (b == (uint32_t)V) ? (int64_t)-1 : (int64_t)b;
+    order[i] = (int64_t)(k & mask);
+  }
+}
+
 // ---------------------------------------------------------------- cross-entropy
 // Per row: lse, loss_row = lse - x[label] (0 if ignored), and
 // dlogits = (softmax - onehot) / n_valid  (n_valid from device memory).
@@ -810,9 +854,32 @@ void embedding_bwd(torch::Tensor tok, torch::Tensor dout, torch::Tensor acc) {
   const c10::cuda::CUDAGuard g(dout.device());
   const int M = (int)tok.numel(), D = (int)acc.size(1), V = (int)acc.size(0);
   if (M == 0) return;
-  auto sorted = at::sort(tok.reshape({-1}), /*stable=*/true, 0, false);
-  auto st_tok = std::get<0>(sorted).contiguous();
-  auto order = std::get<1>(sorted).contiguous();
+  // own single-CTA sort while the keys fit 32 bits and the array fits shared memory
+  // (every training shape here: <= 32768 tokens, vocabulary < 2^17); beyond that
+  // the library's stable radix sort
+  int shift = 0;
+  while ((1L << shift) < M) ++shift;
+  int npow2 = 1;
+  while (npow2 < M) npow2 <<= 1;
+  torch::Tensor st_tok, order;
+  if (M <= 32768 && ((long)(V + 1) << shift) <= (1L << 32)) {
+    st_tok = torch::empty({M}, tok.options().dtype(at::kLong));
+    order = torch::empty({M}, tok.options().dtype(at::kLong));
+    const int smem = npow2 * 4;
+    static bool cfg = false;
+    if (!cfg) {
+      DTB_CUDA(cudaFuncSetAttribute(sort_tokens_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 32768 * 4));
+      cfg = true;
+    }
+    auto tk = tok.reshape({-1}).to(at::kLong).contiguous();
+    sort_tokens_kernel<<<1, 1024, smem, cur_stream()>>>(tk.data_ptr<int64_t>(), M, V, shift, npow2,
+                                                        st_tok.data_ptr<int64_t>(), order.data_ptr<int64_t>());
+    DTB_LAUNCH_CHECK();
+  } else {
+    auto sorted = at::sort(tok.reshape({-1}), /*stable=*/true, 0, false);
+    st_tok = std::get<0>(sorted).contiguous();
+    order = std::get<1>(sorted).contiguous();
+  }
   embedding_bwd_kernel<<<M, std::min(256, std::max(32, D)), 0, cur_stream()>>>(
       st_tok.data_ptr<int64_t>(), order.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
       acc.data_ptr<float>(), M, D, V);

@@ -38,6 +38,11 @@ def attention_reference(qkv: torch.Tensor, batch: int, seqlen: int, nq: int, nkv
     return o.transpose(1, 2).reshape(batch * seqlen, nq * hd)
 
 
+# head sizes with a native kernel: tcgen05/TMEM for 64 and 128 at seq_len % 128 == 0,
+# mma.sync for the rest (any seq_len)
+KERNEL_HEAD_DIMS = (16, 32, 64, 128)
+
+
 class _FlashAttnFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, qkv, batch, seqlen, nq, nkv, hd):  # type: ignore[override]
@@ -60,6 +65,8 @@ def causal_attention(qkv: torch.Tensor, batch: int, seqlen: int, n_q_heads: int,
     """``qkv: [b*s, (nq + 2 nkv) * hd]`` -> ``o: [b*s, nq * hd]``."""
     if n_q_heads % n_kv_heads:
         raise ValueError(f"{n_q_heads} query heads are not a multiple of {n_kv_heads} kv heads")
-    if not qkv.is_cuda or dropout_p > 0.0:
+    if not qkv.is_cuda or dropout_p > 0.0 or head_dim not in KERNEL_HEAD_DIMS:
+        # attention dropout (the shipped configs train with 0.0) and head sizes without a
+        # kernel run PyTorch's SDPA, the reference's own kernel (src/model/attention.py:147)
         return attention_reference(qkv, batch, seqlen, n_q_heads, n_kv_heads, head_dim, dropout_p)
     return _FlashAttnFn.apply(qkv.contiguous(), batch, seqlen, n_q_heads, n_kv_heads, head_dim)

@@ -150,6 +150,11 @@ class FullyShardedModel(nn.Module):
         self.cfg = cfg
         self.policy = build_mixed_precision(cfg)
         self.device = device or (ctx.device if ctx is not None else torch.device("cpu"))
+        if self.device.type == "cuda" and self.policy.param_dtype != torch.bfloat16:
+            raise ValueError(
+                f"parallel.param_dtype={cfg.param_dtype}: the CUDA kernels compute in bf16 (fp32 master "
+                "weights, fp32 gradient reduction); set parallel.param_dtype: bfloat16 for GPU runs "
+                "(float32 compute runs on the CPU/gloo path only)")
         dims = ctx.dims if ctx is not None else None
         self.dp_size = dims.dp_size if dims else 1
         self.dp_rank = dims.dp_rank if dims else 0

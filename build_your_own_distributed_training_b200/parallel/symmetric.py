@@ -159,10 +159,17 @@ class PeerComm:
         if self.heap is not None:
             self._step_barrier()
 
+    # parameter all-gathers on the copy engines (no SM work beside the GEMMs) unless
+    # DTB_AG_COPY_ENGINE=0 selects the SM pull kernel
+    ag_copy_engine = os.environ.get("DTB_AG_COPY_ENGINE", "1") != "0"
+
     def all_gather(self, out_full: torch.Tensor, shard: torch.Tensor) -> None:
         assert self.heap is not None
         nbytes = shard.numel() * shard.element_size()
-        native().peer_all_gather(self.heap.bases, self.heap.offset_of(shard), nbytes, out_full)
+        if self.ag_copy_engine:
+            native().peer_all_gather_ce(self.heap.bases, self.heap.offset_of(shard), nbytes, out_full)
+        else:
+            native().peer_all_gather(self.heap.bases, self.heap.offset_of(shard), nbytes, out_full)
 
     # the reduce-scatter also leaves per-block partial sums of squares of its result
     norm_partials = True
@@ -182,6 +189,52 @@ class PeerComm:
 
     def all_reduce_sum(self, t: torch.Tensor, group: dist.ProcessGroup | None) -> None:
         dist.all_reduce(t, group=group)
+
+
+class PeerReplicaComm(PeerComm):
+    """NO_SHARD over the NVLink transport: every rank keeps whole units, and the
+    gradient all-reduce runs in place in the heap-resident gradient buffers as a
+    reduce-scatter (rank r sums slice r of every rank's buffer into its own, rank
+    order, 1/dp fused) followed by a copy-engine all-gather of the reduced slices.
+    Peers finish reading a rank's slice before that rank writes gradients again:
+    the step barrier after the optimizer step orders it."""
+
+    name = "peer-replica"
+    norm_partials = False
+
+    def __init__(self, group: dist.ProcessGroup, device: torch.device) -> None:
+        super().__init__(group, device)
+        # the engine's view: one shard holds the whole unit, replicated on `size` ranks
+        self.dp_size, self.dp_rank = self.size, self.rank
+        self.size, self.rank = 1, 0
+        self.rgroup, self.rsize = group, self.dp_size
+
+    def alloc_many(self, specs: list[tuple[int, torch.dtype]]) -> list[torch.Tensor]:
+        out = super().alloc_many(specs)
+        self._ag_barrier = _Barrier(self.heap)
+        return out
+
+    def all_gather(self, out_full: torch.Tensor, shard: torch.Tensor) -> None:
+        if out_full.data_ptr() != shard.data_ptr():
+            out_full.copy_(shard)
+
+    def reduce_scatter_mean(self, out_shard: torch.Tensor, full: torch.Tensor, world: int,
+                            part: torch.Tensor | None = None, split: int = 0, rep_w: float = 1.0) -> None:
+        assert self.heap is not None and out_shard.data_ptr() == full.data_ptr()
+        n, d = full.numel(), self.dp_size
+        if n % (4 * d) != 0:  # slices must stay 16-byte aligned: plain all-reduce for this unit
+            dist.all_reduce(full, group=self.group)
+            full.div_(world)
+            return
+        per = n // d
+        off = self.heap.offset_of(full)
+        self._rs_barrier()  # every rank's gradients of this unit are complete
+        # slice r of every rank, summed into this rank's own slice r (each element is read
+        # by the thread that then overwrites it; peers read only their own slices)
+        mine = full[self.dp_rank * per:(self.dp_rank + 1) * per]
+        native().peer_reduce_scatter(self.heap.bases, off, self.dp_rank, 1.0 / world, mine, None, 0, 1.0)
+        self._ag_barrier()  # every slice reduced
+        native().peer_all_gather_ce(self.heap.bases, off, per * 4, full, per * 4, self.dp_rank)
 
 
 # ----------------------------------------------------------------------------- TP
@@ -390,7 +443,13 @@ def build_comms(ctx: Any, config: Any) -> tuple[TPComm | None, PeerComm | None]:
         tokens = config.data.micro_batch_size * config.data.seq_len
         tp = TPComm(ctx.tp_group, dev, tokens, config.model.d_model)
         tp._sequence_parallel = bool(config.parallel.sequence_parallel)
-    if ctx.dims.dp_size > 1 and config.parallel.sharding_strategy in ("FULL_SHARD", "SHARD_GRAD_OP") \
-            and ctx.dims.dp_size <= 8:
-        dp = PeerComm(ctx.dp_group, dev)
+    strategy = config.parallel.sharding_strategy
+    dp_size = ctx.dims.dp_size
+    # HYBRID_SHARD shards inside a node: on one node that is the whole dp group
+    one_node = max(1, ctx.env.local_world_size // ctx.dims.tp_size) >= dp_size
+    if 1 < dp_size <= 8:
+        if strategy in ("FULL_SHARD", "SHARD_GRAD_OP") or (strategy == "HYBRID_SHARD" and one_node):
+            dp = PeerComm(ctx.dp_group, dev)
+        elif strategy == "NO_SHARD" and one_node:
+            dp = PeerReplicaComm(ctx.dp_group, dev)
     return tp, dp

@@ -115,10 +115,12 @@ def main():
     # (tp, sequence parallel, loss parallel): pure TP, TP+SP, pure ZeRO, vocabulary-parallel loss,
     # and at 4+ GPUs the 2-D layout tp2 x dp(world/2), where the ZeRO pull transport and the
     # TP-fused GEMMs run in the same step
-    layouts = [(world, False, False), (world, True, False), (1, False, False), (world, False, True)]
+    layouts = [(world, False, False, "FULL_SHARD"), (world, True, False, "FULL_SHARD"),
+               (1, False, False, "FULL_SHARD"), (world, False, True, "FULL_SHARD"),
+               (1, False, False, "NO_SHARD"), (1, False, False, "HYBRID_SHARD")]
     if world >= 4:
-        layouts += [(2, False, False), (2, True, True)]
-    for tp, sp, lp in layouts:
+        layouts += [(2, False, False, "FULL_SHARD"), (2, True, True, "FULL_SHARD"), (2, False, False, "NO_SHARD")]
+    for tp, sp, lp, strategy in layouts:
         ctx = build_process_context(tp, backend="nccl", verbose=False)
         for fused in (True, False):
             cfg = TrainingConfig.from_yaml(os.path.join(root, "config", "test_tiny.yaml"))
@@ -129,6 +131,7 @@ def main():
             cfg.parallel.tp_size = tp
             cfg.parallel.sequence_parallel = sp
             cfg.parallel.loss_parallel = lp
+            cfg.parallel.sharding_strategy = strategy
             cfg.parallel.param_dtype = "bfloat16"
             cfg.backend = "nccl"
             cfg.kernels.fused_comm = fused
@@ -140,19 +143,21 @@ def main():
                 wdw, _ = tr._next_window()
                 m = train_step(tr.model, wdw, tr.optimizer, tr.scheduler, ctx, cfg)
                 steps.append((m.loss, m.grad_norm))
-            results[(tp, sp, lp, fused)] = steps
+            results[(tp, sp, lp, strategy, fused)] = steps
             # every rank reports the same loss and norm
             t = torch.tensor([v for st in steps for v in st], device=dev, dtype=torch.float64)
             every = [torch.empty_like(t) for _ in range(world)]
             dist.all_gather(every, t)
-            check(all(torch.equal(every[0], e) for e in every), f"tp={tp} sp={sp} lp={lp} fused={fused}: ranks disagree")
-        sf, sn = results[(tp, sp, lp, True)], results[(tp, sp, lp, False)]
+            check(all(torch.equal(every[0], e) for e in every),
+                  f"tp={tp} sp={sp} lp={lp} {strategy} fused={fused}: ranks disagree")
+        sf, sn = results[(tp, sp, lp, strategy, True)], results[(tp, sp, lp, strategy, False)]
+        tag = f"tp={tp} sp={sp} lp={lp} {strategy}"
         for i, ((lf, gf), (ln, gn)) in enumerate(zip(sf, sn)):
-            check(abs(lf - ln) < 1e-3 * (i + 1), f"tp={tp} sp={sp} lp={lp} step {i}: loss fused {lf} vs nccl {ln}")
-            check(abs(gf - gn) < 1e-2 * max(1.0, gn), f"tp={tp} sp={sp} lp={lp} step {i}: grad norm {gf} vs {gn}")
+            check(abs(lf - ln) < 1e-3 * (i + 1), f"{tag} step {i}: loss fused {lf} vs nccl {ln}")
+            check(abs(gf - gn) < 1e-2 * max(1.0, gn), f"{tag} step {i}: grad norm {gf} vs {gn}")
     # the vocabulary-parallel loss equals the replicated-head loss on the same data
     for fused in (True, False):
-        a, b = results[(world, False, True, fused)], results[(world, False, False, fused)]
+        a, b = results[(world, False, True, "FULL_SHARD", fused)], results[(world, False, False, "FULL_SHARD", fused)]
         check(abs(a[0][0] - b[0][0]) < 1e-3, f"loss_parallel first loss {a[0][0]} vs replicated head {b[0][0]}")
     torch.cuda.synchronize()
     check(native().device_error() == 0, "device error word set after training")

@@ -391,7 +391,10 @@ def _attn_ref(qkv, b, s, nq, nkv, hd):
 
 
 @pytest.mark.parametrize("b,s,nq,nkv,hd", [(2, 128, 4, 4, 128), (1, 256, 8, 2, 64), (2, 192, 4, 1, 128),
-                                           (1, 1024, 2, 2, 128)])
+                                           (1, 1024, 2, 2, 128),
+                                           # head sizes and ragged lengths of the mma.sync kernels
+                                           (4, 64, 4, 2, 16), (2, 96, 4, 2, 16), (3, 200, 4, 4, 32),
+                                           (2, 77, 2, 1, 64), (1, 130, 4, 2, 128), (2, 1, 2, 2, 32)])
 def test_attention_fwd_bwd(b, s, nq, nkv, hd):
     from build_your_own_distributed_training_b200.ops.attention import causal_attention
     qkv = _rand(b * s, (nq + 2 * nkv) * hd).requires_grad_()

@@ -224,6 +224,32 @@ def case_cross_entropy():
     return lambda: native().cross_entropy_fwd(logits, labels, -100), 0, 2 * (T // 2) * V * 4
 
 
+def case_ce_fused_fwd():
+    # head GEMM with the log-sum-exp epilogue + row reduce + mean: 4096 tokens, V = 32000
+    from build_your_own_distributed_training_b200.ops import loss as L
+    h, w = _bf(T // 2, D), _bf(V, D)
+    labels = torch.randint(0, V, (T // 2,), device=DEV)
+    return lambda: L.fused_ce_forward(h, w, labels, 0, V), 2 * (T // 2) * V * D, 0
+
+
+def case_ce_fused_bwd():
+    # recomputed head GEMM writing bf16 logit-gradient chunks + dgrad + wgrad GEMMs
+    from build_your_own_distributed_training_b200.ops import loss as L
+    h, w = _bf(T // 2, D), _bf(V, D)
+    labels = torch.randint(0, V, (T // 2,), device=DEV)
+    _, lse, inv_n = L.fused_ce_forward(h, w, labels, 0, V)
+    dloss = torch.ones((), device=DEV)
+    mg = torch.zeros(V * D, device=DEV)
+    return (lambda: L.fused_ce_backward(h, w, labels, lse, inv_n, dloss, 0, V, mg)), 3 * 2 * (T // 2) * V * D, 0
+
+
+def case_sort_tokens():
+    tok = torch.randint(0, V, (T,), device=DEV)
+    dout = _bf(T, D)
+    acc = torch.zeros(V, D, device=DEV)
+    return lambda: native().embedding_bwd(tok, dout, acc), 0, 0
+
+
 def case_adamw():
     n = 96 << 20
     p, g = torch.randn(n, device=DEV), torch.randn(n, device=DEV)
