@@ -246,6 +246,22 @@ void peer_barrier(std::vector<int64_t> bases, int64_t flag_off, int64_t rank, in
   DTB_LAUNCH_CHECK();
 }
 
+// flag word `rank` at flag_off of every rank's heap := epoch (release, system scope),
+// after everything earlier on the stream (e.g. the copy that staged this rank's rows)
+__global__ void peer_signal_kernel(PeerPtrs peers, long flag_off, int rank, int size, uint32_t epoch) {
+  const int p = threadIdx.x;
+  if (p < size) {
+    __threadfence_system();
+    dtb::st_release_sys(reinterpret_cast<uint32_t*>(peers.base[p] + flag_off) + rank, epoch);
+  }
+}
+
+void peer_signal(std::vector<int64_t> bases, int64_t flag_off, int64_t rank, int64_t epoch) {
+  auto peers = make_peers(bases);
+  peer_signal_kernel<<<1, 32, 0, cs()>>>(peers, flag_off, (int)rank, (int)bases.size(), (uint32_t)epoch);
+  DTB_LAUNCH_CHECK();
+}
+
 void peer_all_gather(std::vector<int64_t> bases, int64_t src_off, int64_t shard_bytes, torch::Tensor out) {
   DTB_CHECK(shard_bytes % 16 == 0 && src_off % 16 == 0, "all-gather needs 16-byte aligned shards");
   DTB_CHECK(out.numel() * out.element_size() >= shard_bytes * (long)bases.size(), "all-gather output too small");

@@ -34,6 +34,8 @@
 #include <cudaTypedefs.h>
 #include <torch/extension.h>
 
+#include <cmath>
+
 #include "common.cuh"
 
 bool dtb_debug_enabled();
@@ -89,6 +91,21 @@ struct GemmArgs {
   const float* ce_inv_n;  // device scalar 1 / (number of valid labels)
   const float* acc_in;    // EPI_ACC_BF16OUT: fp32 [M, N] with row stride ld_acc
   long ld_acc;
+  // fp32 outputs: the K range split over `ksplit` work units per tile (see splitk_wait)
+  int ksplit;
+  int* sk_flags;
+  uint32_t sk_epoch;
+  // AG (all-gather fused in front of the GEMM, sequence parallelism): A is the
+  // gathered [M, K] buffer `ag_out`, filled by the kernel's copier warps from this
+  // rank's rows `ag_local` and the peers' staged rows (peer_base[p] + stage_off)
+  const __nv_bfloat16* ag_local;
+  __nv_bfloat16* ag_out;
+  int ag_rows;            // rows per rank (a multiple of the tile height)
+  int ag_mrot;            // m-blocks of this rank's rows: tiles start there
+  long ag_staged_off;     // per-rank "rows staged" flags inside every heap
+  uint32_t ag_epoch;      // this call's epoch (staged flags)
+  uint32_t* ag_count;     // per-128-row chunk: rows copied, cumulative over launches
+  uint32_t ag_target;     // count a chunk reaches once this launch has copied it
 };
 
 constexpr int BM = 128;
@@ -383,6 +400,63 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
   }
 }
 
+// ---------------------------------------------------------------- split-K (fp32 outputs)
+// When the output has too few tiles to fill the SMs evenly (e.g. 256 CTA-pair
+// tiles on 74 pairs is 3.46 waves), each tile's K range is cut into `ksplit`
+// parts, work unit u = split * num_tiles + tile.  Split 0 stores (or
+// accumulates, EPI_ACC_F32) its partial product as usual; split s > 0 waits
+// until split s-1 of the same (tile, quadrant) has published, then adds its
+// partial into D.  The additions happen in split order, so the result is the
+// same on every run.  Flags are per (CTA-tile, quadrant) in a device buffer;
+// split s publishes sk_epoch + s (the host advances sk_epoch by ksplit per
+// launch, so old values never satisfy a wait).  Split s waits on a unit with a
+// smaller index, which every CTA reaches first, so the waits always end.
+__device__ __forceinline__ void splitk_publish(const GemmArgs& a, int ftile, int quad, int lane, int split) {
+  __syncwarp();
+  if (lane == 0) {
+    __threadfence();
+    st_release_sys(reinterpret_cast<uint32_t*>(a.sk_flags) + (long)ftile * 4 + quad, a.sk_epoch + split);
+  }
+}
+
+__device__ __forceinline__ bool splitk_wait(const GemmArgs& a, int ftile, int quad, int split) {
+  return wait_flag(reinterpret_cast<const uint32_t*>(a.sk_flags) + (long)ftile * 4 + quad, a.sk_epoch + split - 1,
+                   a.timeout_ns, a.err);
+}
+
+// split s > 0: D += this split's partial (D read around L1: other SMs wrote it)
+template <int BN>
+__device__ __forceinline__ void splitk_accumulate(const GemmArgs& a, uint32_t tbase, int mb, int nb, int quad,
+                                                  int lane) {
+  const int row = mb * BM + quad * 32 + lane;
+  const uint32_t trow = tbase + ((uint32_t)(quad * 32) << 16);
+  const int n0 = nb * BN;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    if (n0 + c >= a.N) break;
+    float v[32];
+    tmem_ld32(trow + c, v);
+    if (row < a.M) {
+      if (a.alpha != nullptr) {
+        const float sc = *a.alpha;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] *= sc;
+      }
+      float* p = reinterpret_cast<float*>(a.D) + (long)row * a.ldd + n0 + c;
+      const int nv = min(32, a.N - (n0 + c));
+      if (nv >= 32) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 q = __ldcg(reinterpret_cast<const float4*>(p + i));
+          *reinterpret_cast<float4*>(p + i) = make_float4(q.x + v[i], q.y + v[i + 1], q.z + v[i + 2], q.w + v[i + 3]);
+        }
+      } else {
+        for (int i = 0; i < nv; ++i) p[i] = __ldcg(p + i) + v[i];
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- GEMM -> all-reduce
 // Phase 1 (TMEM still held): this thread's row of the tile -> bf16 in the
 // local staging area of the symmetric heap (same [M, N] layout as D).
@@ -580,6 +654,103 @@ __device__ __forceinline__ bool peer_ar_fetch(const GemmArgs& a, int tile, int m
   return true;
 }
 
+// ---------------------------------------------------------------- all-gather -> GEMM
+// Copier warps (AG launches only: warps 10 and 11) pull the gathered A rows in
+// the order the tiles need them (this rank's rows first, then the following
+// ranks'), one 8 KB-class row per warp step, 16-byte loads that bypass L1 (a
+// peer's rows come over NVLink), all issued before any store.  After a row is
+// stored each lane fences its generic stores against the async (TMA) proxy,
+// and lane 0 adds 1 to the row's 128-row chunk counter with release
+// semantics; the producer warp waits (acquire, bounded) until the chunks of a
+// tile's A rows have all their rows, then loads them by TMA.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ bool ag_copy_rows(const GemmArgs& a, int copier, int ncopiers, int lane) {
+  const int M = a.M, K = a.K;
+  const int R = a.ag_rows;
+  const int nranks = a.peer_n;
+  uint32_t staged_seen = 0;  // bit p: rank p's rows are staged
+  const uint32_t* staged = reinterpret_cast<const uint32_t*>(a.peer_base[a.peer_rank] + a.ag_staged_off);
+  for (int rr = copier; rr < M; rr += ncopiers) {
+    // rotated row order: rank r's rows first
+    const int row = (rr + a.peer_rank * R) % M;
+    const int p = row / R;
+    const __nv_bfloat16* src;
+    if (p == a.peer_rank) {
+      src = a.ag_local + (long)(row - p * R) * K;
+    } else {
+      if (!(staged_seen & (1u << p))) {
+        if (!wait_flag(staged + p, a.ag_epoch, a.timeout_ns, a.err)) return false;
+        staged_seen |= 1u << p;
+      }
+      src = reinterpret_cast<const __nv_bfloat16*>(a.peer_base[p] + a.stage_off) + (long)(row - p * R) * K;
+    }
+    __nv_bfloat16* dst = a.ag_out + (long)row * K;
+    // K bf16 = K/8 16-byte pieces per row; 32 lanes, up to 8 pieces each in flight
+    for (int c0 = lane * 8; c0 < K; c0 += 32 * 8 * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = c0 + i * 256;
+        v[i] = c < K ? ld_cg_v4(src + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = c0 + i * 256;
+        if (c < K) *reinterpret_cast<uint4*>(dst + c) = v[i];
+      }
+    }
+    fence_proxy_async_global();
+    __syncwarp();
+    if (lane == 0) red_release_add(a.ag_count + row / 128, 1u);
+  }
+  return true;
+}
+
+// Tile order.  Normal launches: groups of GROUP_M row blocks (L2 reuse of B).
+// All-gather launches: one row block at a time across all column blocks,
+// starting at this rank's own rows, so the tiles consume gathered rows in the
+// order and at about the rate the copier warps deliver them (B, the weight, is
+// small enough to stay in L2 across row blocks).
+template <bool AG>
+__device__ __forceinline__ void ag_or_grouped_coords(const GemmArgs& a, int tile, int& mb, int& nb) {
+  if constexpr (AG) {
+    mb = (tile / a.n_blocks + a.ag_mrot) % a.m_blocks;
+    nb = tile % a.n_blocks;
+  } else {
+    tile_coords(tile, a.m_blocks, a.n_blocks, mb, nb);
+  }
+}
+
+// producer side: every 128-row chunk of rows [row0, row0 + rows) complete
+__device__ __forceinline__ bool ag_wait_rows(const GemmArgs& a, int row0, int rows) {
+  for (int c = row0 / 128; c < (row0 + rows + 127) / 128 && c * 128 < a.M; ++c) {
+    const uint32_t* p = a.ag_count + c;
+    if ((int32_t)(ld_acquire_gpu(p) - a.ag_target) < 0) {
+      const uint64_t t0 = globaltimer_ns();
+      while ((int32_t)(ld_acquire_gpu(p) - a.ag_target) < 0) {
+        if (globaltimer_ns() - t0 > a.timeout_ns) {
+          atomicExch(a.err, ERR_PEER_TIMEOUT);
+          return false;
+        }
+        __nanosleep(128);
+      }
+    }
+  }
+  fence_proxy_async_global();
+  return true;
+}
+
 // ---------------------------------------------------------------- kernel
 // PAIR = false: one CTA per 128 x BN tile.
 // PAIR = true (BN = 256): a (2,1,1) cluster computes a 256 x 256 tile with
@@ -591,10 +762,11 @@ __device__ __forceinline__ bool peer_ar_fetch(const GemmArgs& a, int tile, int m
 // loads count on the leader's "full" barrier; the leader's commits arrive on
 // both CTAs' "empty" / "accumulator full" barriers; both CTAs' epilogue warps
 // arrive on the leader's "accumulator empty" barrier.
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool PAIR>
-__global__ void __launch_bounds__(320, 1)
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool PAIR, bool AG = false>
+__global__ void __launch_bounds__(AG ? 384 : 320, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const GemmArgs args) {
+  static_assert(!AG || (!A_MN && !B_MN), "all-gather mode gathers K-major A rows");
   static_assert(!PAIR || BN == 256, "CTA pairs use 256-column tiles");
   using L = SmemLayout<BN, STAGES, PAIR>;
   constexpr int TILE_M = PAIR ? 2 * BM : BM;
@@ -653,11 +825,21 @@ __global__ void __launch_bounds__(320, 1)
       bool issued[STAGES];
       for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_phase[s] = 0;
       bool ok = true;
-      for (int tile = unit; tile < args.num_tiles && ok; tile += units) {
+      const int kper = (args.k_iters + args.ksplit - 1) / args.ksplit;
+      for (int u = unit; u < args.num_tiles * args.ksplit && ok; u += units) {
+        const int tile = u % args.num_tiles, split = u / args.num_tiles;
         int mb, nb;
-        tile_coords(tile, args.m_blocks, args.n_blocks, mb, nb);
+        ag_or_grouped_coords<AG>(args, tile, mb, nb);
         const int arow = mb * TILE_M + (int)cta * BM;  // first A row this CTA loads
-        for (int k = 0; k < args.k_iters; ++k) {
+        const int k_end = min(args.k_iters, (split + 1) * kper);
+        if constexpr (AG) {
+          if (!ag_wait_rows(args, arow, BM)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+        }
+        for (int k = split * kper; k < k_end; ++k) {
           if (*abort_flag || !mbar_wait(&empty[stage], phase ^ 1, args.err)) {
             *abort_flag = 1;
             ok = false;
@@ -720,7 +902,10 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t phase = 0;
       int t = 0;
       bool ok = true;
-      for (int tile = unit; tile < args.num_tiles && ok; tile += units, ++t) {
+      const int kper = (args.k_iters + args.ksplit - 1) / args.ksplit;
+      for (int u = unit; u < args.num_tiles * args.ksplit && ok; u += units, ++t) {
+        const int split = u / args.num_tiles;
+        const int k_begin = split * kper, k_end = min(args.k_iters, (split + 1) * kper);
         const int acc = t & 1;
         const uint32_t acc_phase = (t >> 1) & 1;
         if (*abort_flag || !mbar_wait(&acc_empty[acc], acc_phase ^ 1, args.err)) {
@@ -729,7 +914,7 @@ __global__ void __launch_bounds__(320, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
-        for (int k = 0; k < args.k_iters; ++k) {
+        for (int k = k_begin; k < k_end; ++k) {
           if (*abort_flag || !mbar_wait(&full[stage], phase, args.err)) {
             *abort_flag = 1;
             ok = false;
@@ -742,8 +927,8 @@ __global__ void __launch_bounds__(320, 1)
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t ad = A_MN ? sdesc_sw128(a0 + kk * 2048, 8192, 1024) : sdesc_sw128(a0 + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? sdesc_sw128(b0 + kk * 2048, 8192, 1024) : sdesc_sw128(b0 + kk * 32, 16, 1024);
-            if constexpr (PAIR) umma_bf16_pair(d, ad, bd, IDESC, (k | kk) != 0);
-            else umma_bf16(d, ad, bd, IDESC, (k | kk) != 0);
+            if constexpr (PAIR) umma_bf16_pair(d, ad, bd, IDESC, (k != k_begin) || kk != 0);
+            else umma_bf16(d, ad, bd, IDESC, (k != k_begin) || kk != 0);
           }
           if constexpr (PAIR) umma_commit_pair(&empty[stage]);
           else umma_commit(&empty[stage]);
@@ -753,6 +938,8 @@ __global__ void __launch_bounds__(320, 1)
         else umma_commit(&acc_full[acc]);
       }
     }
+  } else if (AG && warp >= 10) {
+    if (!ag_copy_rows(args, (int)blockIdx.x * 2 + (warp - 10), (int)gridDim.x * 2, lane)) *abort_flag = 1;
   } else {
     // two epilogue warpgroups (warps 2-9): group g drains the tiles that land
     // in TMEM buffer g, so each group has two tiles of time for its stores
@@ -762,12 +949,13 @@ __global__ void __launch_bounds__(320, 1)
     int t = 0;
     int pend_tile = -1, pend_mb = 0, pend_nb = 0;  // EPI_PEER_AR: tile published, not yet reduced
     int pend2_tile = -1, pend2_mb = 0, pend2_nb = 0;  // two-shot: reduced by its owner, not yet copied
-    for (int tile = unit; tile < args.num_tiles; tile += units, ++t) {
+    for (int u = unit; u < args.num_tiles * args.ksplit; u += units, ++t) {
+      const int tile = u % args.num_tiles, split = u / args.num_tiles;
       const int acc = t & 1;
       if (acc != wg) continue;
       const uint32_t acc_phase = (t >> 1) & 1;
       int mb, nb;
-      tile_coords(tile, args.m_blocks, args.n_blocks, mb, nb);
+      ag_or_grouped_coords<AG>(args, tile, mb, nb);
       const int slab = PAIR ? 2 * mb + (int)cta : mb;     // this CTA's 128-row block of the output
       const int ftile = PAIR ? 2 * tile + (int)cta : tile;
       if (*abort_flag || !mbar_wait(&acc_full[acc], acc_phase, args.err)) {
@@ -777,6 +965,15 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_after();
       if constexpr (EPI == EPI_PEER_AR) {
         peer_ar_stage<BN>(args, tmem_base + acc * BN, slab, nb, quad, lane);
+      } else if constexpr (EPI == EPI_STORE_F32 || EPI == EPI_ACC_F32) {
+        if (split == 0) {
+          epilogue_tile<BN, EPI>(args, tmem_base + acc * BN, slab, nb, quad, lane);
+        } else if (splitk_wait(args, ftile, quad, split)) {
+          splitk_accumulate<BN>(args, tmem_base + acc * BN, slab, nb, quad, lane);
+        } else {
+          *abort_flag = 1;
+        }
+        if (args.ksplit > 1) splitk_publish(args, ftile, quad, lane, split);
       } else {
         epilogue_tile<BN, EPI>(args, tmem_base + acc * BN, slab, nb, quad, lane);
       }
@@ -880,22 +1077,24 @@ static CUtensorMap make_map(const void* base, long inner, long rows, long row_st
 
 static int num_sms() { return device_sm_count(); }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool PAIR>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool PAIR, bool AG = false>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t st) {
   using L = SmemLayout<BN, STAGES, PAIR>;
-  auto kern = gemm_tcgen05_kernel<BN, STAGES, A_MN, B_MN, EPI, PAIR>;
+  auto kern = gemm_tcgen05_kernel<BN, STAGES, A_MN, B_MN, EPI, PAIR, AG>;
+  constexpr int NT = AG ? 384 : 320;
   static bool configured = false;
   if (!configured) {
     DTB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
     configured = true;
   }
   if (g.num_tiles == 0) return;
+  const int work = g.num_tiles * std::max(1, g.ksplit);
   if constexpr (PAIR) {
     // persistent (2,1,1) clusters, one per pair of SMs
-    const int pairs = std::min(g.num_tiles, num_sms() / 2);
+    const int pairs = std::min(work, num_sms() / 2);
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
-    cfg.blockDim = dim3(320, 1, 1);
+    cfg.blockDim = dim3(NT, 1, 1);
     cfg.dynamicSmemBytes = L::TOTAL;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -907,8 +1106,8 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cu
     cfg.numAttrs = 1;
     DTB_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, g));
   } else {
-    const int grid = std::min(g.num_tiles, num_sms());
-    kern<<<grid, 320, L::TOTAL, st>>>(ta, tb, g);
+    const int grid = std::min(work, num_sms());
+    kern<<<grid, NT, L::TOTAL, st>>>(ta, tb, g);
   }
   DTB_LAUNCH_CHECK();
 }
@@ -946,6 +1145,80 @@ static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, 
   }
 }
 
+// all-gather -> GEMM launches (K-major operands; the epilogues the column-parallel
+// layers use)
+template <int BN, bool PAIR>
+static void dispatch_epi_ag(int epi, const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t st) {
+  constexpr int ST = (BN == 256 && !PAIR) ? 4 : 6;
+  switch (epi) {
+    case EPI_STORE_BF16: launch<BN, ST, false, false, EPI_STORE_BF16, PAIR, true>(ta, tb, g, st); break;
+    case EPI_ROPE: launch<BN, ST, false, false, EPI_ROPE, PAIR, true>(ta, tb, g, st); break;
+    case EPI_SWIGLU:
+      if constexpr (BN == 256) { launch<BN, ST, false, false, EPI_SWIGLU, PAIR, true>(ta, tb, g, st); break; }
+      TORCH_CHECK(false, "swiglu epilogue needs BN=256");
+    default: DTB_CHECK(false, "all-gather GEMM: epilogue %d not built", epi);
+  }
+}
+
+// Split-K for fp32 outputs: the number of K parts per tile, chosen so the work
+// units fill the persistent grid's waves (DTB_GEMM_KSPLIT=n forces n, 1 = off).
+static int choose_ksplit(int tiles, int units_per_wave, int k_iters) {
+  static int forced = -2;
+  if (forced == -2) {
+    const char* e = getenv("DTB_GEMM_KSPLIT");
+    forced = (e != nullptr && atoi(e) > 0) ? atoi(e) : -1;
+  }
+  auto eff = [&](int ks) {
+    const double w = (double)tiles * ks / units_per_wave;
+    return w / std::ceil(w);
+  };
+  if (forced > 0) {
+    int ks = std::max(1, std::min(forced, k_iters));
+    while (ks > 1 && (long)(ks - 1) * ((k_iters + ks - 1) / ks) >= k_iters) --ks;  // no empty part
+    return ks;
+  }
+  if (eff(1) >= 0.92) return 1;
+  int best = 1;
+  double best_score = eff(1);
+  for (int ks = 2; ks <= 4; ++ks) {
+    if (k_iters / ks < 16) break;  // keep each part deep enough to fill the pipeline
+    const double score = eff(ks) - 0.03 * (ks - 1);  // each extra part re-reads and re-writes D
+    if (score > best_score + 0.02) best = ks, best_score = score;
+  }
+  return best;
+}
+
+// Per-device flag words of the split-K handshake (allocated once, never freed)
+// and the launch epoch.
+static int* splitk_flags(long needed, uint32_t* epoch_out, int ks) {
+  constexpr long kFlags = 1L << 20;
+  static int* flags[64] = {nullptr};
+  static uint32_t epoch[64] = {0};
+  int dev = 0;
+  DTB_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64 || needed > kFlags) return nullptr;
+  if (flags[dev] == nullptr) {
+    DTB_CUDA(cudaMalloc(&flags[dev], kFlags * sizeof(int)));
+    DTB_CUDA(cudaMemset(flags[dev], 0, kFlags * sizeof(int)));
+    epoch[dev] = 1;
+  }
+  *epoch_out = epoch[dev];
+  epoch[dev] += (uint32_t)ks;
+  return flags[dev];
+}
+
+// Per-device chunk counters of the all-gather GEMM (allocated once, never freed;
+// cleared on the stream before each launch).
+static uint32_t* ag_counters(long chunks) {
+  constexpr long kMax = 1L << 16;
+  static uint32_t* cnt[64] = {nullptr};
+  int dev = 0;
+  DTB_CUDA(cudaGetDevice(&dev));
+  DTB_CHECK(dev >= 0 && dev < 64 && chunks <= kMax, "all-gather GEMM: %ld row chunks (max %ld)", chunks, kMax);
+  if (cnt[dev] == nullptr) DTB_CUDA(cudaMalloc(&cnt[dev], kMax * sizeof(uint32_t)));
+  return cnt[dev];
+}
+
 // CTA pairs for 256-column tiles unless DTB_GEMM_PAIR=0 (single-CTA tiles)
 static bool pair_enabled() {
   static int v = -1;
@@ -971,6 +1244,17 @@ struct PeerCfg {
   bool two_shot = false;
 };
 
+// All-gather fused in front of the GEMM (sequence parallelism, column-parallel layers).
+struct AgCfg {
+  std::vector<int64_t> bases;
+  int rank;
+  long stage_off, staged_off;
+  uint32_t epoch;
+  double timeout_s;
+  const __nv_bfloat16* local;
+  int rows;  // rows per rank
+};
+
 // Fused LM-head cross-entropy epilogues (EPI_CE_STATS / EPI_CE_GRAD).
 struct CeCfg {
   const int64_t* labels;
@@ -985,7 +1269,7 @@ static void gemm_impl(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_
                       c10::optional<torch::Tensor> R, c10::optional<torch::Tensor> alpha,
                       c10::optional<torch::Tensor> cos_t, c10::optional<torch::Tensor> sin_t,
                       c10::optional<torch::Tensor> D2, int64_t p0, int64_t p1, const PeerCfg* peer,
-                      const CeCfg* ce = nullptr) {
+                      const CeCfg* ce = nullptr, const AgCfg* ag = nullptr) {
   using namespace dtb;
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && D.is_cuda(), "gemm: CUDA tensors expected");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm: bf16 operands expected");
@@ -1100,6 +1384,40 @@ static void gemm_impl(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_
   g.k_iters = (int)((K + BK - 1) / BK);
   g.num_tiles = g.m_blocks * g.n_blocks;
   g.flag_tiles = pair ? 2 * g.num_tiles : g.num_tiles;
+  if (ag != nullptr) {
+    DTB_CHECK(!a_mn && !b_mn && (e == EPI_STORE_BF16 || e == EPI_ROPE || e == EPI_SWIGLU) && peer == nullptr,
+              "all-gather GEMM: K-major operands and a store / RoPE / SwiGLU epilogue");
+    DTB_CHECK(ag->bases.size() >= 2 && ag->bases.size() <= (size_t)MAX_PEERS && ag->rows > 0 &&
+                  (long)ag->rows * (long)ag->bases.size() == M && ag->rows % tile_m == 0 && K % 8 == 0 &&
+                  ag->stage_off % 16 == 0,
+              "all-gather GEMM: %d rows per rank x %zu ranks must equal M=%ld, in %d-row tiles", ag->rows,
+              ag->bases.size(), M, tile_m);
+    for (size_t i = 0; i < ag->bases.size(); ++i) g.peer_base[i] = reinterpret_cast<uint8_t*>(ag->bases[i]);
+    g.peer_n = (int)ag->bases.size();
+    g.peer_rank = ag->rank;
+    g.stage_off = ag->stage_off;
+    g.ag_staged_off = ag->staged_off;
+    g.ag_epoch = ag->epoch;
+    g.timeout_ns = (uint64_t)(ag->timeout_s * 1e9);
+    g.ag_local = ag->local;
+    g.ag_out = reinterpret_cast<__nv_bfloat16*>(A.data_ptr());
+    g.ag_rows = ag->rows;
+    g.ag_mrot = (int)((long)ag->rank * ag->rows / tile_m);
+    g.ag_count = ag_counters((M + 127) / 128);
+    g.ag_target = 128;
+    DTB_CUDA(cudaMemsetAsync(g.ag_count, 0, ((M + 127) / 128) * sizeof(uint32_t), at::cuda::getCurrentCUDAStream()));
+  }
+  g.ksplit = 1;
+  if ((e == EPI_STORE_F32 || e == EPI_ACC_F32) && peer == nullptr && ce == nullptr && g.num_tiles > 0) {
+    const int ks = choose_ksplit(g.num_tiles, pair ? num_sms() / 2 : num_sms(), g.k_iters);
+    if (ks > 1) {
+      g.sk_flags = splitk_flags((long)g.flag_tiles * 4, &g.sk_epoch, ks);
+      if (g.sk_flags != nullptr) {
+        g.ksplit = ks;
+        g.timeout_ns = 10ull * 1000000000ull;
+      }
+    }
+  }
   if (e == EPI_CE_STATS) {
     TORCH_CHECK(D.scalar_type() == at::kFloat && D.size(0) == M && D.size(1) == 2L * g.n_blocks,
                 "gemm: ce stats must be fp32 [M, 2 * n_blocks]");
@@ -1114,6 +1432,12 @@ static void gemm_impl(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_
   const CUtensorMap ta = a_mn ? make_map(A.data_ptr(), M, K, A.stride(0), BK) : make_map(A.data_ptr(), K, M, A.stride(0), BM);
   const CUtensorMap tb = b_mn ? make_map(B.data_ptr(), NB, K, B.stride(0), BK) : make_map(B.data_ptr(), K, NB, B.stride(0), 128);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (ag != nullptr) {
+    if (BN == 256 && pair) dispatch_epi_ag<256, true>(e, ta, tb, g, st);
+    else if (BN == 256) dispatch_epi_ag<256, false>(e, ta, tb, g, st);
+    else dispatch_epi_ag<128, false>(e, ta, tb, g, st);
+    return;
+  }
   if (BN == 256 && pair) {
     if (!a_mn && !b_mn) dispatch_epi<256, false, false, true>(e, ta, tb, g, st);
     else if (!a_mn && b_mn) dispatch_epi<256, false, true, true>(e, ta, tb, g, st);
@@ -1206,4 +1530,23 @@ void gemm_ce_grad(torch::Tensor h, torch::Tensor w, torch::Tensor labels, torch:
           lse.data_ptr<float>(), inv_n.data_ptr<float>()};
   gemm_impl(h, w, out, false, false, dtb::EPI_CE_GRAD, c10::nullopt, dloss, c10::nullopt, c10::nullopt,
             c10::nullopt, 0, 0, nullptr, &c);
+}
+
+// Column-parallel GEMM with the sequence-parallel all-gather fused in front of it:
+// A_gathered [size * rows, K] is filled by the kernel (this rank's rows from
+// A_local, every peer's from its heap at stage_off once the peer has raised its
+// staged flag to `epoch`) and multiplied as it lands; D = A_gathered x B^T with
+// the given epilogue (store, RoPE, SwiGLU: as gemm_entry).
+void gemm_ag(torch::Tensor A_gathered, torch::Tensor A_local, torch::Tensor B, torch::Tensor D, int64_t epi,
+             c10::optional<torch::Tensor> cos_t, c10::optional<torch::Tensor> sin_t, c10::optional<torch::Tensor> D2,
+             int64_t p0, int64_t p1, std::vector<int64_t> bases, int64_t rank, int64_t stage_off, int64_t staged_off,
+             int64_t epoch, double timeout_s) {
+  TORCH_CHECK(A_local.scalar_type() == at::kBFloat16 && A_local.is_contiguous() && A_local.dim() == 2 &&
+                  A_local.size(1) == A_gathered.size(1) &&
+                  (reinterpret_cast<uintptr_t>(A_local.data_ptr()) & 15) == 0,
+              "gemm_ag: bf16 contiguous local rows");
+  AgCfg c{bases, (int)rank, (long)stage_off, (long)staged_off, (uint32_t)epoch, timeout_s,
+          reinterpret_cast<const __nv_bfloat16*>(A_local.data_ptr()), (int)A_local.size(0)};
+  gemm_impl(A_gathered, B, D, false, false, epi, c10::nullopt, c10::nullopt, cos_t, sin_t, D2, p0, p1, nullptr,
+            nullptr, &c);
 }

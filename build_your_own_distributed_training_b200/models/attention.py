@@ -40,7 +40,9 @@ class Attention(nn.Module):
         """``x``: ``[b, s, d]`` (or local ``[tokens, d]`` under sequence parallelism)."""
         out_shape = x.shape if residual is None else residual.shape
         seqlen = cos.shape[0]
-        x2, grad_comm = tpar.column_input_fused(x.reshape(-1, x.shape[-1]), self.tp)
+        # under sequence parallelism x2 may stay this rank's rows: the QKV GEMM gathers them
+        x2, grad_comm = tpar.column_input_fused(x.reshape(-1, x.shape[-1]), self.tp,
+                                                sp_ok=self.wq.bias is None)
         hd = self.head_dim
         nq, nkv = self.wq.weight.shape[0] // hd, self.wk.weight.shape[0] // hd
         if self.wq.bias is not None:
@@ -53,7 +55,7 @@ class Attention(nn.Module):
         else:
             w, mg = fused_rows([self.wq.weight, self.wk.weight, self.wv.weight])
             qkv = linear_qkv_rope(x2, w, cos, sin, nq, nkv, hd, seqlen, main_grad=mg, grad_comm=grad_comm)
-        o = causal_attention(qkv, x2.shape[0] // seqlen, seqlen, nq, nkv, hd,
+        o = causal_attention(qkv, qkv.shape[0] // seqlen, seqlen, nq, nkv, hd,
                              self.dropout_p if self.training else 0.0)
         r2 = residual.reshape(-1, residual.shape[-1]) if residual is not None else None
         y = tpar.row_output_linear(o, self.wo.weight, r2, self.tp,

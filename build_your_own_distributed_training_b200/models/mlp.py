@@ -29,7 +29,8 @@ class SwiGLUMLP(nn.Module):
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
         out_shape = x.shape if residual is None else residual.shape
-        x2, grad_comm = tpar.column_input_fused(x.reshape(-1, x.shape[-1]), self.tp)
+        x2, grad_comm = tpar.column_input_fused(x.reshape(-1, x.shape[-1]), self.tp,
+                                                sp_ok=self.gate_proj.bias is None)
         ffn = self.gate_proj.weight.shape[0]
         if self.gate_proj.bias is not None:
             g = F.linear(x2, self.gate_proj.weight.to(x2.dtype), self.gate_proj.bias.to(x2.dtype))

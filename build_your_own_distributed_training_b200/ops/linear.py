@@ -76,10 +76,23 @@ def linear(x: torch.Tensor, weight: torch.Tensor, *, bias: torch.Tensor | None =
     return y + bias if bias is not None else y
 
 
+def _is_sp(grad_comm) -> bool:
+    return getattr(grad_comm, "sp", False)
+
+
 class _QKVRopeFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, cos, sin, rope_cols, head_dim, seqlen, main_grad, grad_comm):  # type: ignore[override]
         x2 = _flat(x)
+        if _is_sp(grad_comm):
+            # x2: this rank's token rows; the GEMM gathers the others' as it goes
+            y, x2 = grad_comm.comm.gather_gemm(x2, weight, gemm.EPI_ROPE, cos=cos, sin=sin, p0=rope_cols,
+                                               p1=head_dim * 65536 + seqlen)
+            ctx.save_for_backward(x2, weight, cos, sin)
+            ctx.cfg = (rope_cols, head_dim, seqlen)
+            ctx.main_grad = main_grad
+            ctx.grad_comm = grad_comm
+            return y
         if x2.is_cuda:
             y = gemm.mm_nt_rope(x2, weight, cos, sin, rope_cols, head_dim, seqlen)
         else:
@@ -98,7 +111,10 @@ class _QKVRopeFn(torch.autograd.Function):
         d = _flat(dy).contiguous().clone()
         rope_backward_(d, cos, sin, rope_cols, head_dim, seqlen)
         wc = w if d.is_cuda else w.to(d.dtype)
-        dx = _input_grad(d, wc, ctx.grad_comm).view(*dy.shape[:-1], w.shape[1])
+        if _is_sp(ctx.grad_comm):
+            dx = ctx.grad_comm.comm.dgrad_reduce_scatter(d, wc)
+        else:
+            dx = _input_grad(d, wc, ctx.grad_comm).view(*dy.shape[:-1], w.shape[1])
         dw = _weight_grad(d, x2, w, ctx.main_grad)
         return dx, dw, None, None, None, None, None, None, None
 
@@ -141,6 +157,15 @@ class _SwiGLUFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, ffn, main_grad, grad_comm):  # type: ignore[override]
         x2 = _flat(x)
+        if _is_sp(grad_comm) and ffn % 128 == 0:
+            (act, gu), x2 = grad_comm.comm.gather_gemm(x2, weight, gemm.EPI_SWIGLU, ffn=ffn)
+            ctx.save_for_backward(x2, weight, gu)
+            ctx.ffn = ffn
+            ctx.main_grad = main_grad
+            ctx.grad_comm = grad_comm
+            return act
+        if _is_sp(grad_comm):  # no SwiGLU epilogue for this width: gather first, then the plain path
+            x2 = grad_comm.comm.all_gather_rows(x2)
         if x2.is_cuda and ffn % 128 == 0:
             act, gu = gemm.mm_nt_swiglu(x2, weight, ffn)
         else:
@@ -159,7 +184,10 @@ class _SwiGLUFn(torch.autograd.Function):
         x2, w, gu = ctx.saved_tensors
         dgu = swiglu_backward(_flat(dact), gu, ctx.ffn)
         wc = w if dgu.is_cuda else w.to(dgu.dtype)
-        dx = _input_grad(dgu, wc, ctx.grad_comm).view(*dact.shape[:-1], w.shape[1])
+        if _is_sp(ctx.grad_comm):
+            dx = ctx.grad_comm.comm.dgrad_reduce_scatter(dgu, wc)
+        else:
+            dx = _input_grad(dgu, wc, ctx.grad_comm).view(*dact.shape[:-1], w.shape[1])
         dw = _weight_grad(dgu, x2, w, ctx.main_grad)
         return dx, dw, None, None, None
 

@@ -315,6 +315,7 @@ class TPComm:
         self.heap = SymmetricHeap(group, 2 * slot + self.flag_bytes + 64 * 1024, device)
         self.slots = [self.heap.alloc(slot), self.heap.alloc(slot)]
         self.flag_off = self.heap.alloc(self.flag_bytes)
+        self.ag_flag_off = self.heap.alloc(256)  # per-rank "rows staged" flags of the fused all-gather GEMM
         self.barrier = _Barrier(self.heap)
         self.calls = 0
 
@@ -379,6 +380,52 @@ class TPComm:
         return _RowParallelAR.apply(x2.contiguous(), weight, residual, main_grad, self)
 
     _sequence_parallel = False
+
+    # ---- sequence parallelism: column-parallel GEMMs with the token all-gather fused in
+    # front (forward) and the input gradient fused with its reduce-scatter (backward)
+    def sp_fusable(self, x_local: torch.Tensor) -> bool:
+        R, K = x_local.shape
+        return (R % 256 == 0 and R * self.size <= self.max_tokens and K <= self.width and K % 8 == 0
+                and x_local.dtype == torch.bfloat16)
+
+    def _stage_rows(self, x_local: torch.Tensor) -> int:
+        off = self._slot()
+        self._staging(off, tuple(x_local.shape)).copy_(x_local)
+        native().peer_signal(self.heap.bases, self.ag_flag_off, self.rank, self.calls)
+        return off
+
+    def gather_gemm(self, x_local: torch.Tensor, w: torch.Tensor, epi: int, *, cos=None, sin=None, p0: int = 0,
+                    p1: int = 0, ffn: int = 0) -> tuple[Any, torch.Tensor]:
+        """``(y, x_gathered)``: ``y = all_gather_rows(x_local) @ w^T`` with the given epilogue
+        (0 store, 4 RoPE, 5 SwiGLU: ``y = (act, [g|u])``), the gather inside the GEMM."""
+        x_local = x_local.contiguous()
+        R, K = x_local.shape
+        M = R * self.size
+        off = self._stage_rows(x_local)
+        xg = torch.empty(M, K, device=x_local.device, dtype=x_local.dtype)
+        if epi == 5:
+            act = torch.empty(M, ffn, device=x_local.device, dtype=x_local.dtype)
+            gu = torch.empty(M, 2 * ffn, device=x_local.device, dtype=x_local.dtype)
+            native().gemm_ag(xg, x_local, w, act, 5, None, None, gu, ffn, 0, self.heap.bases, self.rank, off,
+                             self.ag_flag_off, self.calls, TIMEOUT_S)
+            return (act, gu), xg
+        out = torch.empty(M, w.shape[0], device=x_local.device, dtype=x_local.dtype)
+        native().gemm_ag(xg, x_local, w, out, epi, cos, sin, None, p0, p1, self.heap.bases, self.rank, off,
+                         self.ag_flag_off, self.calls, TIMEOUT_S)
+        return out, xg
+
+    def dgrad_reduce_scatter(self, dy: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """This rank's rows of ``sum over the group of dy @ w`` (``w``: ``[N, K]``) in one kernel."""
+        M, K = dy.shape[0], w.shape[1]
+        if M > self.max_tokens or K > self.width:
+            raise ValueError(f"input gradient [{M}, {K}] exceeds the TP staging area "
+                             f"[{self.max_tokens}, {self.width}]")
+        rows = M // self.size
+        out = torch.empty(rows, K, device=dy.device, dtype=torch.bfloat16)
+        off = self._slot()
+        native().gemm_peer_rs(dy.contiguous(), w, out, True, None, self.heap.bases, self.rank, off, self.flag_off,
+                              self.calls, TIMEOUT_S, self.rank * rows, rows)
+        return out
 
     # per-row records exchanged by the fused vocabulary-parallel cross-entropy
     def exchange_rows(self, rows: int, row_bytes: int) -> tuple[int, torch.Tensor]:

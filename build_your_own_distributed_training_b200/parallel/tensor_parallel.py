@@ -264,13 +264,29 @@ def sequence_slice(t: torch.Tensor, tp: TPInfo | None) -> torch.Tensor:
     return t[tp.rank * rows:(tp.rank + 1) * rows]
 
 
-def column_input_fused(x2: torch.Tensor, tp: TPInfo | None) -> tuple[torch.Tensor, Any]:
+class SPColumn:
+    """Marks a column-parallel layer's transport under sequence parallelism: the layer
+    receives this rank's token rows and runs the all-gather inside its GEMM
+    (``TPComm.gather_gemm``) and the input gradient's reduce-scatter inside its dgrad
+    GEMM (``TPComm.dgrad_reduce_scatter``)."""
+
+    sp = True
+
+    def __init__(self, comm: Any) -> None:
+        self.comm = comm
+
+
+def column_input_fused(x2: torch.Tensor, tp: TPInfo | None, sp_ok: bool = True) -> tuple[torch.Tensor, Any]:
     """Like :func:`column_input`, but when the NVLink transport can fuse the
     input-gradient all-reduce into the column-parallel layer's dgrad GEMM,
-    return ``(x2, transport)`` for the layer to do so (no separate f-op)."""
-    if (tp is not None and tp.size > 1 and tp.fused and tp.comm is not None and x2.is_cuda
-            and not tp.sequence_parallel):
-        return x2, tp.comm
+    return ``(x2, transport)`` for the layer to do so (no separate f-op).  Under
+    sequence parallelism it returns this rank's rows and an :class:`SPColumn`:
+    the gather and the gradient's reduce-scatter are fused into the layer's GEMMs."""
+    if tp is not None and tp.size > 1 and tp.fused and tp.comm is not None and x2.is_cuda:
+        if not tp.sequence_parallel:
+            return x2, tp.comm
+        if sp_ok and hasattr(tp.comm, "sp_fusable") and tp.comm.sp_fusable(x2):
+            return x2, SPColumn(tp.comm)
     return column_input(x2, tp), None
 
 

@@ -66,7 +66,7 @@ def main():
     check(float(part[-3:].abs().sum()) == 0.0, "reduce-scatter wrote past its blocks")
 
     # ---- TP transport
-    M, K, N = 1024, 512, 768
+    M, K, N = max(1024, 256 * world), 512, 768  # 256-row slices per rank for the fused SP GEMMs
     tpc = symmetric.TPComm(g, dev, M, N)
     x = torch.randn(M, K, device=dev).to(torch.bfloat16)
     w = (torch.randn(N, K, device=dev) * 0.05).to(torch.bfloat16)
@@ -89,6 +89,20 @@ def main():
         ref = torch.empty(rows, N, device=dev)
         dist.reduce_scatter_tensor(ref, part)
         check(rel(y, ref + res_rs.float()) < 1e-2, f"fused GEMM+reduce-scatter mismatch (call {it})")
+    # sequence parallelism: all-gather fused in front of the GEMM, dgrad fused with the reduce-scatter
+    xl = torch.randn(M // world, K, device=dev).to(torch.bfloat16)
+    for it in range(2):
+        y, xg = tpc.gather_gemm(xl, w[:N], 0)
+        ref_g = torch.empty(M, K, device=dev, dtype=torch.bfloat16)
+        dist.all_gather_into_tensor(ref_g, xl)
+        check(torch.equal(xg, ref_g), f"fused all-gather GEMM: gathered rows differ (call {it})")
+        check(rel(y, gemm.mm_nt(ref_g, w)) < 1e-2, f"fused all-gather GEMM mismatch (call {it})")
+        dy = torch.randn(M, N, device=dev).to(torch.bfloat16)
+        dxl = tpc.dgrad_reduce_scatter(dy, w)
+        full = gemm.mm_nn(dy, w).float()
+        ref_rs = torch.empty(M // world, K, device=dev)
+        dist.reduce_scatter_tensor(ref_rs, full)
+        check(rel(dxl, ref_rs) < 1e-2, f"fused dgrad reduce-scatter mismatch (call {it})")
     a = torch.randn(M, N, device=dev).to(torch.bfloat16)
     ar = tpc.all_reduce(a)
     ref_ar = a.float().clone()
@@ -126,8 +140,10 @@ def main():
             cfg = TrainingConfig.from_yaml(os.path.join(root, "config", "test_tiny.yaml"))
             cfg.model.vocab_size, cfg.model.d_model, cfg.model.n_layers = 1024, 512, 2
             cfg.model.n_heads, cfg.model.n_kv_heads, cfg.model.ffn_hidden_size = 8, 4, 1024
-            cfg.model.max_seq_len = 256
-            cfg.data.seq_len, cfg.data.micro_batch_size, cfg.data.dataset_path = 256, 2, "uniform"
+            # 1024 tokens per step: 256-row slices per rank up to tp=4, so sequence parallelism
+            # takes the fused all-gather GEMM and dgrad reduce-scatter paths
+            cfg.model.max_seq_len = 512
+            cfg.data.seq_len, cfg.data.micro_batch_size, cfg.data.dataset_path = 512, 2, "uniform"
             cfg.parallel.tp_size = tp
             cfg.parallel.sequence_parallel = sp
             cfg.parallel.loss_parallel = lp

@@ -64,6 +64,30 @@ def test_gemm_tn_accumulate(M, N, K):
     assert _rel(acc, ref) < 1e-5
 
 
+@pytest.mark.parametrize("M,N,K", [(4096, 4096, 4096), (4096, 4096, 2048), (1024, 4096, 8192), (4096, 3072, 4096)])
+def test_gemm_wgrad_split_k_is_exact_order(M, N, K):
+    """Shapes whose tiles under-fill the last wave run the weight-gradient GEMM in K parts
+    added in split order: both epilogues (store, accumulate) match the fp32 oracle, with
+    alpha, and repeat bit for bit."""
+    a, b = _rand(K, M), _rand(K, N)
+    base = torch.randn(M, N, device=DEV)
+    ref = a.float().t() @ b.float()
+    st = torch.empty(M, N, device=DEV)
+    gemm.mm_tn_acc(a, b, st, store=True)
+    assert _rel(st, ref) < 1e-5
+    acc = base.clone()
+    gemm.mm_tn_acc(a, b, acc)
+    assert _rel(acc, base + ref) < 1e-5
+    alpha = torch.tensor([0.5], device=DEV)
+    al = torch.empty(M, N, device=DEV)
+    gemm.mm_tn_acc(a, b, al, alpha=alpha, store=True)
+    assert _rel(al, 0.5 * ref) < 1e-5
+    for _ in range(3):
+        again = base.clone()
+        gemm.mm_tn_acc(a, b, again)
+        assert torch.equal(again, acc)
+
+
 def test_gemm_alpha_and_residual():
     a, b, r = _rand(256, 512), _rand(384, 512), _rand(256, 384)
     alpha = torch.tensor([0.25], device=DEV)
@@ -167,6 +191,47 @@ def test_gemm_peer_allreduce_two_shot_emulated_partner(M, N, K):
     assert (own == 0).any() and (own == 1).any()
     staged0 = heaps[0][:stage].view(BF).view(M, N)
     assert torch.equal(staged0[own == 0], out[own == 0])  # the owner's sum, for the partner to copy
+
+
+@pytest.mark.parametrize("ranks,R,N,K,epi", [(2, 512, 768, 512, "store"), (4, 256, 512, 1024, "store"),
+                                              (2, 1024, 4096, 4096, "store"), (2, 512, 1024, 512, "swiglu"),
+                                              (2, 256, 768, 256, "rope")])
+def test_gemm_all_gather_emulated_peers(ranks, R, N, K, epi):
+    """The all-gather fused in front of the GEMM, rank 0 of `ranks` with the peers emulated by
+    memory: their rows sit staged in their heaps and their staged flags are raised before the
+    launch, so the copier warps pull them while the tiles of rank 0's own rows start."""
+    M = ranks * R
+    x = _rand(M, K)
+    w = _rand(N, K, scale=0.5)
+    stage = R * K * 2
+    staged_off = (stage + 255) // 256 * 256
+    heaps = [torch.zeros(staged_off + 256, device=DEV, dtype=torch.uint8) for _ in range(ranks)]
+    for p in range(1, ranks):
+        heaps[p][:stage].view(BF).copy_(x[p * R:(p + 1) * R].reshape(-1))
+    heaps[0][staged_off:staged_off + 4 * ranks].view(torch.int32).fill_(3)
+    xg = torch.empty(M, K, device=DEV, dtype=BF)
+    bases = [h.data_ptr() for h in heaps]
+    if epi == "store":
+        out = torch.empty(M, N, device=DEV, dtype=BF)
+        native().gemm_ag(xg, x[:R].contiguous(), w, out, 0, None, None, None, 0, 0, bases, 0, 0, staged_off, 3, 2.0)
+        ref = x.float() @ w.float().t()
+    elif epi == "swiglu":
+        F2 = N // 2
+        out = torch.empty(M, F2, device=DEV, dtype=BF)
+        gu = torch.empty(M, N, device=DEV, dtype=BF)
+        native().gemm_ag(xg, x[:R].contiguous(), w, out, 5, None, None, gu, F2, 0, bases, 0, 0, staged_off, 3, 2.0)
+        y = x.float() @ w.float().t()
+        ref = torch.nn.functional.silu(y[:, :F2]) * y[:, F2:]
+    else:
+        from build_your_own_distributed_training_b200.ops.rope import precompute_rope_cache
+        hd, seq = 128, 256
+        cos, sin = precompute_rope_cache(hd, seq, 10000.0, device=DEV)
+        out = torch.empty(M, N, device=DEV, dtype=BF)
+        native().gemm_ag(xg, x[:R].contiguous(), w, out, 4, cos, sin, None, 2 * hd * 2, hd * 65536 + seq, bases, 0,
+                         0, staged_off, 3, 2.0)
+        ref = gemm.mm_nt_rope(x, w, cos, sin, 2 * hd * 2, hd, seq).float()
+    assert torch.equal(xg, x)  # the gathered rows are the GEMM's saved input for the weight gradient
+    assert _rel(out, ref) < 2e-2
 
 
 @pytest.mark.parametrize("M,N,K", [(1024, 768, 512), (4096, 4096, 2048)])
