@@ -193,6 +193,7 @@ def profile_one_step(step_fn, prefixes: tuple[str, ...]) -> tuple[int, dict]:
         torch.cuda.synchronize()
     n = 0
     split: dict[str, float] = {}
+    other: dict[str, float] = {}
     for e in prof.events():
         if e.device_type != torch.autograd.DeviceType.CUDA:
             continue
@@ -207,9 +208,13 @@ def profile_one_step(step_fn, prefixes: tuple[str, ...]) -> tuple[int, dict]:
                 if any(k in low for k in keys):
                     cls = name
                     break
-        split[cls] = split.get(cls, 0.0) + e.time_range.elapsed_us() / 1e3
+        ms = e.time_range.elapsed_us() / 1e3
+        split[cls] = split.get(cls, 0.0) + ms
+        if cls == "other":
+            other[e.name[:60]] = other.get(e.name[:60], 0.0) + ms
     split = {k: round(v, 2) for k, v in sorted(split.items(), key=lambda kv: -kv[1])}
     split["step_ms"] = round(e0.elapsed_time(e1), 2)
+    split["top_other"] = {k: round(v, 2) for k, v in sorted(other.items(), key=lambda kv: -kv[1])[:5]}
     return n, split
 
 

@@ -285,7 +285,8 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int qc = c0 + c + e;
-          float v = ex2_approx(fmaf(__uint_as_float(sr[c + e]), a.scale_log2, Ls[qc] * -LOG2E));
+          const float xe = fmaf(__uint_as_float(sr[c + e]), a.scale_log2, Ls[qc] * -LOG2E);
+          float v = ex2_approx(xe);
           if (diag && q0 + qc < kr) v = 0.f;
           p[e] = v;
           d[e] = v * (__uint_as_float(dr[c + e]) - Ds[qc]);
@@ -528,7 +529,8 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int kc = j * BKV + c0 + c + e;
-          float p = ex2_approx(fmaf(__uint_as_float(sr[c + e]), a.scale_log2, -L2));
+          const float xe = fmaf(__uint_as_float(sr[c + e]), a.scale_log2, -L2);
+          float p = ex2_approx(xe);
           if (diag && kc > qr) p = 0.f;
           d[e] = p * (__uint_as_float(dr[c + e]) - Dr);
         }
@@ -774,7 +776,10 @@ __global__ void __launch_bounds__(320, 1)
       float p[64];
 #pragma unroll
       for (int cc = 0; cc < 64; ++cc) {
-        p[cc] = ex2_approx(fmaf(__uint_as_float(sr[cc >> 5][cc & 31]), a.scale_log2, -L2));
+        {
+          const float xe = fmaf(__uint_as_float(sr[cc >> 5][cc & 31]), a.scale_log2, -L2);
+          p[cc] = ex2_approx(xe);
+        }
         if (diag && j * BKV + c0 + cc > qr) p[cc] = 0.f;
       }
       tmem_wait_ld();

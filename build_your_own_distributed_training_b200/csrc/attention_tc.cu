@@ -18,9 +18,10 @@
 //              through shared memory (a 64-thread named barrier per row
 //              quarter), then runs the online softmax in exp2 form with the
 //              scale folded into one FFMA.  One exponential in four is
-//              evaluated on the FMA pipes (exp2_fma below) instead of the
-//              special-function unit, whose rate (16 per clock per SM) bounds
-//              this stage.  P_j goes in bf16 to one of two shared-memory
+//              evaluated on the FMA pipes (exp2_fma, common.cuh) instead of
+//              the special-function unit (measured: 617 TFLOP/s at b1 s4096
+//              h32 hd128; moving half of them, or the bf16 rounding, to the
+//              FMA/integer pipes was slower, 549).  P_j goes in bf16 to one of two shared-memory
 //              buffers in the 128-byte-swizzled K-major layout the MMA reads
 //              (each thread writes one 64-column atom of its row); with two P
 //              buffers the softmax of tile j only waits for the PV product of
@@ -50,26 +51,6 @@ constexpr float RESCALE_THRESHOLD = 8.f;
 constexpr int SOFTMAX_THREADS = 256;   // warps 2-9
 constexpr int NTHREADS = 64 + SOFTMAX_THREADS;
 
-// 2^x on the FMA/ALU pipes, for x <= RESCALE_THRESHOLD (masked scores are
-// -inf).  Range reduction x = n + f with n = round(x) taken from the mantissa
-// of x + 1.5 * 2^23 (f in [-1/2, 1/2]), 2^f by the degree-3 polynomial that
-// interpolates it at the four Chebyshev nodes of [-1/2, 1/2] (coefficients
-// computed for this kernel; max relative error 1.0e-4, below the 2^-9 of the
-// bf16 P it feeds), and 2^n added to the result's exponent field.  Inputs
-// below -125 are clamped there, which gives a value below 2^-124 (the sums
-// and bf16 P treat it as 0).
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fmaxf(x, -125.f);
-  const float shifter = 12582912.f;  // 1.5 * 2^23
-  const float t = x + shifter;
-  const float n = t - shifter;       // round(x)
-  const float f = x - n;
-  float p = fmaf(0.05583828f, f, 0.24263948f);
-  p = fmaf(p, f, 0.69313675f);
-  p = fmaf(p, f, 0.99992454f);
-  const int e = __float_as_int(t) - __float_as_int(shifter);  // n as an integer
-  return __int_as_float(__float_as_int(p) + (e << 23));
-}
 
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {

@@ -275,6 +275,36 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
 }
+// 2^x on the FMA/ALU pipes, for finite x below 2^7 or -inf (softmax
+// exponents: masked scores are -inf).  Range reduction x = n + f with n = round(x) taken from the mantissa
+// of x + 1.5 * 2^23 (f in [-1/2, 1/2]), 2^f by the degree-3 polynomial that
+// interpolates it at the four Chebyshev nodes of [-1/2, 1/2] (coefficients
+// computed for this kernel; max relative error 1.0e-4, below the 2^-9 of the
+// bf16 P it feeds), and 2^n added to the result's exponent field.  Inputs
+// below -125 are clamped there, which gives a value below 2^-124 (the sums
+// and bf16 P treat it as 0).
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -125.f);
+  const float shifter = 12582912.f;  // 1.5 * 2^23
+  const float t = x + shifter;
+  const float n = t - shifter;       // round(x)
+  const float f = x - n;
+  float p = fmaf(0.05583828f, f, 0.24263948f);
+  p = fmaf(p, f, 0.69313675f);
+  p = fmaf(p, f, 0.99992454f);
+  const int e = __float_as_int(t) - __float_as_int(shifter);  // n as an integer
+  return __int_as_float(__float_as_int(p) + (e << 23));
+}
+
+// bf16x2 of (a, b), a in the low half, on the integer pipes: add half a bf16
+// ulp to the fp32 bit pattern and keep the high halves (one byte permute for
+// the pair), i.e. round half away from zero, which differs from
+// round-to-nearest-even only on exact ties.  No conversion instruction, so it
+// stays off the pipe that also evaluates the exponentials.  Finite inputs.
+__device__ __forceinline__ uint32_t pack_bf16x2_alu(float a, float b) {
+  return __byte_perm(__float_as_uint(a) + 0x8000u, __float_as_uint(b) + 0x8000u, 0x7632);
+}
+
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
   __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&u);
   return __bfloat1622float2(h);

@@ -1160,32 +1160,23 @@ static void dispatch_epi_ag(int epi, const CUtensorMap& ta, const CUtensorMap& t
   }
 }
 
-// Split-K for fp32 outputs: the number of K parts per tile, chosen so the work
-// units fill the persistent grid's waves (DTB_GEMM_KSPLIT=n forces n, 1 = off).
+// Split-K for fp32 outputs: the number of K parts per tile.  Off unless
+// DTB_GEMM_KSPLIT=n asks for n parts.  Measured on B200 (weight-gradient GEMMs,
+// 4096-12288 x 4096-11008, K = 4096): two parts ran at 0.68-0.72x and four at
+// 0.35-0.42x the one-part speed even where one part leaves the last wave 46%
+// full; each extra part's fp32 read-modify-write of D in the epilogue, with
+// half the MMA work per unit to hide it behind, outweighs the filled wave.
 static int choose_ksplit(int tiles, int units_per_wave, int k_iters) {
+  (void)tiles;
+  (void)units_per_wave;
   static int forced = -2;
   if (forced == -2) {
     const char* e = getenv("DTB_GEMM_KSPLIT");
-    forced = (e != nullptr && atoi(e) > 0) ? atoi(e) : -1;
+    forced = (e != nullptr && atoi(e) > 0) ? atoi(e) : 1;
   }
-  auto eff = [&](int ks) {
-    const double w = (double)tiles * ks / units_per_wave;
-    return w / std::ceil(w);
-  };
-  if (forced > 0) {
-    int ks = std::max(1, std::min(forced, k_iters));
-    while (ks > 1 && (long)(ks - 1) * ((k_iters + ks - 1) / ks) >= k_iters) --ks;  // no empty part
-    return ks;
-  }
-  if (eff(1) >= 0.92) return 1;
-  int best = 1;
-  double best_score = eff(1);
-  for (int ks = 2; ks <= 4; ++ks) {
-    if (k_iters / ks < 16) break;  // keep each part deep enough to fill the pipeline
-    const double score = eff(ks) - 0.03 * (ks - 1);  // each extra part re-reads and re-writes D
-    if (score > best_score + 0.02) best = ks, best_score = score;
-  }
-  return best;
+  int ks = std::max(1, std::min(forced, k_iters));
+  while (ks > 1 && (long)(ks - 1) * ((k_iters + ks - 1) / ks) >= k_iters) --ks;  // no empty part
+  return ks;
 }
 
 // Per-device flag words of the split-K handshake (allocated once, never freed)

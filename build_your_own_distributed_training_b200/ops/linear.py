@@ -84,7 +84,10 @@ class _QKVRopeFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, cos, sin, rope_cols, head_dim, seqlen, main_grad, grad_comm):  # type: ignore[override]
         x2 = _flat(x)
-        if _is_sp(grad_comm):
+        if _is_sp(grad_comm) and head_dim % 64 != 0:
+            # no RoPE epilogue for this head size: gather first, then the plain path below
+            x2 = grad_comm.comm.all_gather_rows(x2)
+        elif _is_sp(grad_comm):
             # x2: this rank's token rows; the GEMM gathers the others' as it goes
             y, x2 = grad_comm.comm.gather_gemm(x2, weight, gemm.EPI_ROPE, cos=cos, sin=sin, p0=rope_cols,
                                                p1=head_dim * 65536 + seqlen)
@@ -93,8 +96,11 @@ class _QKVRopeFn(torch.autograd.Function):
             ctx.main_grad = main_grad
             ctx.grad_comm = grad_comm
             return y
-        if x2.is_cuda:
+        if x2.is_cuda and head_dim % 64 == 0:
             y = gemm.mm_nt_rope(x2, weight, cos, sin, rope_cols, head_dim, seqlen)
+        elif x2.is_cuda:  # head sizes the RoPE epilogue does not tile: GEMM, then the RoPE kernel
+            y = gemm.mm_nt(x2, weight)
+            rope_forward(y, cos, sin, rope_cols, head_dim, seqlen)
         else:
             y = gemm.mm_nt(x2, weight.to(x2.dtype))
             rope_forward(y, cos, sin, rope_cols, head_dim, seqlen)

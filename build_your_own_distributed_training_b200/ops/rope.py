@@ -44,6 +44,10 @@ def _heads_view(y: torch.Tensor, rope_cols: int, head_dim: int, seqlen: int) -> 
 def rope_forward(y: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, rope_cols: int,
                  head_dim: int, seqlen: int) -> None:
     """In place on a packed 2-D ``[b*s, cols]`` tensor, first ``rope_cols`` columns."""
+    if y.is_cuda and y.dtype == torch.bfloat16:
+        from ._ext import native
+        native().rope_fwd(y, cos, sin, rope_cols, head_dim, seqlen)
+        return
     v = _heads_view(y, rope_cols, head_dim, seqlen)
     c, s = cos[:seqlen][None, :, None, :], sin[:seqlen][None, :, None, :]
     rot = (v.float() * c + _rotate_half(v.float()) * s).to(y.dtype)

@@ -64,11 +64,28 @@ def test_gemm_tn_accumulate(M, N, K):
     assert _rel(acc, ref) < 1e-5
 
 
-@pytest.mark.parametrize("M,N,K", [(4096, 4096, 4096), (4096, 4096, 2048), (1024, 4096, 8192), (4096, 3072, 4096)])
-def test_gemm_wgrad_split_k_is_exact_order(M, N, K):
-    """Shapes whose tiles under-fill the last wave run the weight-gradient GEMM in K parts
-    added in split order: both epilogues (store, accumulate) match the fp32 oracle, with
-    alpha, and repeat bit for bit."""
+@pytest.mark.parametrize("ks", [2, 3])
+def test_gemm_wgrad_split_k_is_exact_order(ks):
+    """The weight-gradient GEMM in K parts (DTB_GEMM_KSPLIT, read once per process: run in a
+    child process) added in split order: both epilogues (store, accumulate) match the fp32
+    oracle, with alpha, and repeat bit for bit."""
+    import subprocess
+    import sys
+    code = ("import sys; sys.path.insert(0, %r)\n" % os.path.dirname(os.path.dirname(os.path.dirname(
+        os.path.abspath(__file__)))) + "from tests.gpu.test_kernels import _split_k_case\n_split_k_case()\n")
+    r = subprocess.run([sys.executable, "-c", code], env=dict(os.environ, DTB_GEMM_KSPLIT=str(ks)),
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "SPLITK_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+def _split_k_case():
+    for (M, N, K) in [(4096, 4096, 4096), (1024, 4096, 8192), (4096, 3072, 2048)]:
+        _split_k_shape(M, N, K)
+    assert native().device_error() == 0
+    print("SPLITK_OK")
+
+
+def _split_k_shape(M, N, K):
     a, b = _rand(K, M), _rand(K, N)
     base = torch.randn(M, N, device=DEV)
     ref = a.float().t() @ b.float()
