@@ -409,6 +409,318 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// ============================================================== two query tiles per CTA
+// attn_fwd_pp_kernel: one CTA per (pair of adjacent 128-row query tiles, head,
+// batch), so the two tiles share every K/V load and, more importantly, each
+// tile's softmax runs while the tensor cores work on the other tile:
+//   warp 0     TMA: Q_A, Q_B once; K_j into a 2-deep ring, V_j into one stage
+//   warp 1     TMEM (S_A, S_B: 128 columns each; O_A, O_B: hd each) and MMAs
+//              in the order S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) ...
+//   warps 2-5  softmax of tile A (thread = query row, 128 scores), warps 6-9 of
+//              tile B.  P_X goes to one bf16 shared buffer per tile; the
+//              softmax of tile X at step j writes it once PV_X(j-1) has read it.
+// Tile A = 2*pair, tile B = 2*pair + 1: B has one more key tile (its diagonal).
+// Same online softmax as attn_fwd_tc_kernel (exp2 form, stale-max rescale).
+template <int HD>
+struct SmemPP {
+  static constexpr int Q_BYTES = BM * HD * 2;
+  static constexpr int K_BYTES = BN * HD * 2;
+  static constexpr int V_BYTES = BN * HD * 2;
+  static constexpr int P_BYTES = BM * BN * 2;
+  static constexpr int Q_OFF = 0;                         // Q_A, Q_B
+  static constexpr int K_OFF = Q_OFF + 2 * Q_BYTES;       // 2 stages
+  static constexpr int V_OFF = K_OFF + 2 * K_BYTES;       // 1 stage
+  static constexpr int P_OFF = V_OFF + V_BYTES;           // P_A, P_B
+  static constexpr int BAR_OFF = P_OFF + 2 * P_BYTES;
+  static constexpr int N_BARS = 16;
+  static constexpr int TOTAL = BAR_OFF + N_BARS * 8 + 16 + 1024;
+  static_assert(TOTAL <= 232448, "shared memory per CTA");
+};
+
+template <int HD>
+__global__ void __maxnreg__(200)
+    attn_fwd_pp_kernel(const __grid_constant__ CUtensorMap tm_qk, const __grid_constant__ CUtensorMap tm_v,
+                       const FwdArgs a) {
+  using L = SmemPP<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;     // [2]
+  uint64_t* k_empty = bars + 3;    // [2]
+  uint64_t* v_full = bars + 5;
+  uint64_t* v_empty = bars + 6;
+  uint64_t* s_full = bars + 7;     // [2 tiles]
+  uint64_t* p_full = bars + 9;     // [2 tiles]
+  uint64_t* pv_done = bars + 11;   // [2 tiles]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + L::N_BARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int npairs = a.S / (2 * BM);
+  const int pr = npairs - 1 - blockIdx.x;  // longest rows first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (a.nq / a.nkv);
+  const int qb0 = 2 * pr;                  // tile A; tile B = qb0 + 1
+  const int nkb_a = qb0 + 1, nkb_b = qb0 + 2;
+  const int row0 = b * a.S;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_qk);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const uint32_t t_s[2] = {tmem, tmem + 128};
+  const uint32_t t_o[2] = {tmem + 256, tmem + 256 + HD};
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, 2 * L::Q_BYTES);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c)
+          tma_load_2d(sm + L::Q_OFF + t * L::Q_BYTES + c * 16384, &tm_qk, q_full, h * HD + c * 64,
+                      row0 + (qb0 + t) * BM);
+      auto load_k = [&](int j) -> bool {
+        const int st = j & 1;
+        if (*abort_flag || !mbar_wait(&k_empty[st], ((j >> 1) & 1) ^ 1, a.err)) return false;
+        mbar_arrive_expect_tx(&k_full[st], L::K_BYTES);
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c)
+          tma_load_2d(sm + L::K_OFF + st * L::K_BYTES + c * 16384, &tm_qk, &k_full[st], (a.nq + hk) * HD + c * 64,
+                      row0 + j * BN);
+        return true;
+      };
+      bool ok = load_k(0);
+      for (int j = 0; j < nkb_b && ok; ++j) {
+        if (*abort_flag || !mbar_wait(v_empty, (j & 1) ^ 1, a.err)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(v_full, L::V_BYTES);
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+          for (int c = 0; c < HD / 64; ++c)
+            tma_load_2d(sm + L::V_OFF + i * (HD / 64) * 8192 + c * 8192, &tm_v, v_full,
+                        (a.nq + a.nkv + hk) * HD + c * 64, row0 + j * BN + i * 64);
+        if (j + 1 < nkb_b) ok = load_k(j + 1);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_S = idesc_bf16(BM, BN, false, false);
+      constexpr uint32_t ID_O = idesc_bf16(BM, HD, false, true);
+      const uint32_t q0 = smem_u32(sm + L::Q_OFF);
+      const uint32_t p0 = smem_u32(sm + L::P_OFF);
+      const uint32_t v0 = smem_u32(sm + L::V_OFF);
+      bool ok = mbar_wait(q_full, 0, a.err);
+      auto issue_s = [&](int t, int j) -> bool {  // S_t(j) = Q_t K_j^T
+        const int st = j & 1;
+        if (!mbar_wait(&k_full[st], (j >> 1) & 1, a.err)) return false;
+        tc_fence_after();
+        const uint32_t k0 = smem_u32(sm + L::K_OFF + st * L::K_BYTES);
+        const uint32_t qt = q0 + t * L::Q_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_bf16(t_s[t], sdesc_sw128(qt + off, 16, 1024), sdesc_sw128(k0 + off, 16, 1024), ID_S, kk != 0);
+        }
+        umma_commit(&s_full[t]);
+        // K_j is done once tile B (the later user, or the only one past tile A's end) has it
+        if (t == 1 || j >= nkb_a) umma_commit(&k_empty[st]);
+        return true;
+      };
+      auto issue_pv = [&](int t, int j) -> bool {  // O_t += P_t V_j
+        if (!mbar_wait(&p_full[t], j & 1, a.err)) return false;
+        tc_fence_after();
+        const uint32_t pt = p0 + t * L::P_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint32_t pa = pt + (kk >> 2) * 16384 + (kk & 3) * 32;
+          const uint32_t vb = v0 + (kk >> 2) * (HD / 64) * 8192 + (kk & 3) * 2048;
+          umma_bf16(t_o[t], sdesc_sw128(pa, 16, 1024), sdesc_sw128(vb, 8192, 1024), ID_O, (j | kk) != 0);
+        }
+        umma_commit(&pv_done[t]);
+        return true;
+      };
+      if (ok) ok = issue_s(0, 0);
+      if (ok) ok = issue_s(1, 0);
+      for (int j = 0; j < nkb_b && ok && !*abort_flag; ++j) {
+        if (!mbar_wait(v_full, j & 1, a.err)) {
+          ok = false;
+          break;
+        }
+        if (j < nkb_a) {
+          if (!issue_pv(0, j)) {
+            ok = false;
+            break;
+          }
+          if (j + 1 < nkb_a && !issue_s(0, j + 1)) {
+            ok = false;
+            break;
+          }
+        }
+        if (!issue_pv(1, j)) {
+          ok = false;
+          break;
+        }
+        umma_commit(v_empty);  // V_j read by both tiles' products
+        if (j + 1 < nkb_b && !issue_s(1, j + 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warps
+    const int t = (warp - 2) >> 2;           // 0: tile A, 1: tile B
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;          // row within the tile == TMEM lane
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const int qb = qb0 + t;
+    const int nkb = t == 0 ? nkb_a : nkb_b;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkb; ++j) {
+      if (*abort_flag || !mbar_wait(&s_full[t], j & 1, a.err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32_async(t_s[t] + lane_off + c * 32, sr[c]);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_regs(sr[c]);
+      float sv[BN];
+#pragma unroll
+      for (int c = 0; c < BN; ++c) sv[c] = __uint_as_float(sr[c >> 5][c & 31]);
+      if (j == qb) {
+#pragma unroll
+        for (int c = 0; c < BN; ++c)
+          if (c > r) sv[c] = -INFINITY;
+      }
+      float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+      for (int c = 4; c < BN; c += 4) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) mx4[i] = fmaxf(mx4[i], sv[c + i]);
+      }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
+      float alpha = 1.f;
+      bool rescale = false;
+      if (mx > m_used + RESCALE_THRESHOLD) {
+        alpha = (m_used == -INFINITY) ? 0.f : exp2f(m_used - mx);
+        rescale = (m_used != -INFINITY);
+        m_used = mx;
+      }
+      const float neg_m = -m_used;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[BN / 2];
+#pragma unroll
+      for (int c = 0; c < BN; c += 2) {
+        const float x0 = fmaf(sv[c], a.scale_log2, neg_m), x1 = fmaf(sv[c + 1], a.scale_log2, neg_m);
+        float p0, p1;
+        if ((c & 6) == 6) {
+          p0 = exp2_fma(x0);
+          p1 = exp2_fma(x1);
+        } else {
+          p0 = ex2_approx(x0);
+          p1 = ex2_approx(x1);
+        }
+        rs4[(c >> 1) & 3] += p0 + p1;
+        pk[c / 2] = pack_bf16x2(p0, p1);
+      }
+      l = l * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
+      // PV_t(j-1) must be done before O is rescaled and before P_t is rewritten
+      if (j > 0) {
+        if (!mbar_wait(&pv_done[t], (j - 1) & 1, a.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      if (__any_sync(0xffffffffu, rescale)) {
+        const float f = rescale ? alpha : 1.f;
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+          float o[32];
+          tmem_ld32(t_o[t] + lane_off + c, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= f;
+          tmem_st32(t_o[t] + lane_off + c, o);
+        }
+        tmem_st_wait();
+      }
+      uint8_t* P = sm + L::P_OFF + t * L::P_BYTES;
+#pragma unroll
+      for (int ch = 0; ch < BN / 8; ++ch) {
+        const int atom = ch >> 3, cc = ch & 7;
+        uint4 v;
+        v.x = pk[ch * 4 + 0];
+        v.y = pk[ch * 4 + 1];
+        v.z = pk[ch * 4 + 2];
+        v.w = pk[ch * 4 + 3];
+        *reinterpret_cast<uint4*>(P + atom * 16384 + r * 128 + ((cc ^ (r & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+    }
+    if (ok && mbar_wait(&pv_done[t], (nkb - 1) & 1, a.err)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      const long orow = (long)row0 + qb * BM + r;
+      __nv_bfloat16* op = a.out + orow * (long)a.nq * HD + h * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        float o[32];
+        tmem_ld32(t_o[t] + lane_off + c, o);
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 w;
+          w.x = pack_bf16x2(o[i] * inv, o[i + 1] * inv);
+          w.y = pack_bf16x2(o[i + 2] * inv, o[i + 3] * inv);
+          w.z = pack_bf16x2(o[i + 4] * inv, o[i + 5] * inv);
+          w.w = pack_bf16x2(o[i + 6] * inv, o[i + 7] * inv);
+          *reinterpret_cast<uint4*>(op + c + i) = w;
+        }
+      }
+      a.lse[((long)b * a.nq + h) * a.S + qb * BM + r] = (m_used + log2f(l)) / LOG2E;
+    } else {
+      *abort_flag = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -439,6 +751,17 @@ static CUtensorMap qkv_map(const void* base, long rows, long cols, int box_rows)
   return m;
 }
 
+// two query tiles per CTA when the sequence has an even number of 128-row tiles
+// (DTB_ATTN_FWD_PP=0 keeps one tile per CTA)
+static bool pp_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("DTB_ATTN_FWD_PP");
+    v = (e == nullptr || e[0] != '0') ? 1 : 0;
+  }
+  return v == 1;
+}
+
 template <int HD>
 void fwd_tc_launch(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse, int B, int S, int nq, int nkv,
                    float scale) {
@@ -446,6 +769,20 @@ void fwd_tc_launch(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& ls
   const long rows = (long)B * S, cols = (long)(nq + 2 * nkv) * HD;
   const CUtensorMap tqk = qkv_map(qkv.data_ptr(), rows, cols, 128);
   const CUtensorMap tv = qkv_map(qkv.data_ptr(), rows, cols, 64);
+  if (S % (2 * BM) == 0 && pp_enabled()) {
+    using LP = SmemPP<HD>;
+    static bool cfg_pp = false;
+    if (!cfg_pp) {
+      DTB_CUDA(cudaFuncSetAttribute(attn_fwd_pp_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, LP::TOTAL));
+      cfg_pp = true;
+    }
+    FwdArgs args{reinterpret_cast<__nv_bfloat16*>(o.data_ptr()), lse.data_ptr<float>(), S, nq, nkv, scale * LOG2E,
+                 dtb_error_word()};
+    attn_fwd_pp_kernel<HD><<<dim3(S / (2 * BM), nq, B), 320, LP::TOTAL, at::cuda::getCurrentCUDAStream()>>>(tqk, tv,
+                                                                                                            args);
+    DTB_LAUNCH_CHECK();
+    return;
+  }
   static bool cfg = false;
   if (!cfg) {
     DTB_CUDA(cudaFuncSetAttribute(attn_fwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
