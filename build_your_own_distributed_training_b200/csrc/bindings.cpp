@@ -44,6 +44,7 @@ void peer_all_reduce_bf16(std::vector<int64_t> bases, int64_t src_off, c10::opti
 void peer_reduce_rows_bf16(std::vector<int64_t> bases, int64_t src_off, int64_t row0, int64_t cols, torch::Tensor out);
 void wait_flag_probe(torch::Tensor flag, int64_t target, double timeout_s);
 int64_t gemm_ce_blocks(int64_t N);
+torch::Tensor tmem_a_operand_check(torch::Tensor A, torch::Tensor B);
 void gemm_ag(torch::Tensor A_gathered, torch::Tensor A_local, torch::Tensor B, torch::Tensor D, int64_t epi,
              c10::optional<torch::Tensor> cos_t, c10::optional<torch::Tensor> sin_t, c10::optional<torch::Tensor> D2,
              int64_t p0, int64_t p1, std::vector<int64_t> bases, int64_t rank, int64_t stage_off, int64_t staged_off,
@@ -101,6 +102,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_reduce_rows_bf16", &peer_reduce_rows_bf16);
   m.def("wait_flag_probe", &wait_flag_probe, "bounded wait on a flag (tests the timeout path)");
   m.def("gemm_ce_blocks", &gemm_ce_blocks, "column blocks of the fused cross-entropy statistics");
+  m.def("tmem_a_operand_check", &tmem_a_operand_check, "one tcgen05 MMA with its A operand in tensor memory");
   m.def("gemm_ag", &gemm_ag, "sequence-parallel all-gather fused in front of the tcgen05 GEMM");
   m.def("peer_signal", &peer_signal, "raise this rank's flag to `epoch` in every peer's heap");
   m.def("gemm_ce_stats", &gemm_ce_stats, "head GEMM -> per-block log-sum-exp statistics and target logits");

@@ -105,6 +105,14 @@ def _split_k_shape(M, N, K):
         assert torch.equal(again, acc)
 
 
+def test_tmem_a_operand_layout():
+    """tcgen05 MMA reading A from tensor memory in the softmax threads' layout (row = lane,
+    bf16 pairs per 32-bit column) equals the fp32 product."""
+    a, b = _rand(128, 128), _rand(128, 128)
+    d = native().tmem_a_operand_check(a, b)
+    assert _rel(d, a.float() @ b.float().t()) < 1e-5
+
+
 def test_gemm_alpha_and_residual():
     a, b, r = _rand(256, 512), _rand(384, 512), _rand(256, 384)
     alpha = torch.tensor([0.25], device=DEV)
