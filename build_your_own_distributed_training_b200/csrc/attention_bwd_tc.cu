@@ -341,6 +341,290 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// ============================================================== dK / dV, P in TMEM
+// attn_bwd_dkdv_tm_kernel: CTA per (128-key tile, kv head, batch), 128-query
+// tiles (every MMA 128 x 128 or 128 x hd wide instead of the 64-query
+// kernel's 128 x 64), with P^T and dS^T kept in tensor memory as the A
+// operands of the dV / dK products, so they need no shared memory:
+//   TMEM  S^T [0,128) | dP^T [128,256) | dV [256, 256+hd) | dK [256+hd, 256+2hd)
+//   The elementwise threads (two per key row, 64 queries each) read their
+//   S^T / dP^T columns and write P^T / dS^T as bf16 pairs over the first 32
+//   of those same columns, so nothing another thread still has to read is
+//   overwritten.  MMA order per query tile: S^T, dP^T, then (once P^T is
+//   written) dV += P^T dO, then (once dS^T is written) dK += dS^T Q; the next
+//   tile's S^T / dP^T are issued after these, and the tensor pipe runs its
+//   operations in issue order, so they overwrite P^T / dS^T only after use.
+//   The exponentials of tile i overlap its dP^T product, the dS^T products its
+//   dV product.  Q / dO / lse / D: 2-deep ring.  Warp 0 loads, warp 1 owns
+//   TMEM and issues MMAs, warps 2-9 the elementwise part.  Bounded waits.
+__device__ __forceinline__ void umma_bf16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+template <int HD>
+struct SmKVT {
+  static constexpr int KV_TILE = 128 * HD * 2;   // K or V: [hd/64][128 rows][128 B]
+  static constexpr int QT = 128 * HD * 2;        // Q or dO tile: [hd/64][128 rows][128 B]
+  static constexpr int NS = 2;
+  static constexpr int K_OFF = 0;
+  static constexpr int V_OFF = K_OFF + KV_TILE;
+  static constexpr int Q_OFF = V_OFF + KV_TILE;
+  static constexpr int O_OFF = Q_OFF + NS * QT;
+  static constexpr int LD_OFF = O_OFF + NS * QT;     // NS x (lse[128], D[128]) floats
+  static constexpr int BAR_OFF = LD_OFF + NS * 1024;
+  static constexpr int N_BARS = 16;
+  static constexpr int TOTAL = BAR_OFF + N_BARS * 8 + 16 + 1024;
+  static_assert(TOTAL <= 232448, "shared memory per CTA");
+};
+
+template <int HD>
+__global__ void __launch_bounds__(320, 1)
+    attn_bwd_dkdv_tm_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_q,
+                            const __grid_constant__ CUtensorMap tm_do, const BwdArgs a) {
+  using L = SmKVT<HD>;
+  constexpr int BKV = 128, BQ = 128, NS = L::NS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR_OFF);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* q_full = bars + 1;   // [NS]
+  uint64_t* q_empty = bars + 3;  // [NS]
+  uint64_t* s_full = bars + 5;   // S^T of the current tile
+  uint64_t* dp_full = bars + 6;  // dP^T of the current tile
+  uint64_t* pt_full = bars + 7;  // P^T written (256 arrivals)
+  uint64_t* ds_full = bars + 8;  // dS^T written (256 arrivals)
+  uint64_t* g_done = bars + 9;   // dV / dK products of the tile finished
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + L::N_BARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkb = a.S / BKV;
+  const int kb = nkb - 1 - blockIdx.x;  // tiles near the end have the least work: start the others first
+  const int hk = blockIdx.y, b = blockIdx.z;
+  const int grp = a.nq / a.nkv;
+  const int kv0 = kb * BKV;
+  const int nqt = a.S / BQ - kb;        // query tiles from the diagonal one
+  const int total = nqt * grp;
+  const int row0 = b * a.S;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(dp_full, 1);
+    mbar_init(pt_full, 256);
+    mbar_init(ds_full, 256);
+    mbar_init(g_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const uint32_t t_s = tmem, t_dp = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 256 + HD;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * L::KV_TILE);
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c) {
+        tma_load_2d(sm + L::K_OFF + c * 16384, &tm_kv, kv_full, (a.nq + hk) * HD + c * 64, row0 + kv0);
+        tma_load_2d(sm + L::V_OFF + c * 16384, &tm_kv, kv_full, (a.nq + a.nkv + hk) * HD + c * 64, row0 + kv0);
+      }
+      for (int it = 0; it < total; ++it) {
+        const int st = it % NS;
+        if (*abort_flag || !mbar_wait(&q_empty[st], ((it / NS) & 1) ^ 1, a.err)) {
+          *abort_flag = 1;
+          break;
+        }
+        const int hh = hk * grp + it / nqt;
+        const int q0 = (kb + it % nqt) * BQ;
+        mbar_arrive_expect_tx(&q_full[st], 2 * L::QT + 1024);
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c) {
+          tma_load_2d(sm + L::Q_OFF + st * L::QT + c * 16384, &tm_q, &q_full[st], hh * HD + c * 64, row0 + q0);
+          tma_load_2d(sm + L::O_OFF + st * L::QT + c * 16384, &tm_do, &q_full[st], hh * HD + c * 64, row0 + q0);
+        }
+        const long li = ((long)b * a.nq + hh) * a.S + q0;
+        bulk_load(sm + L::LD_OFF + st * 1024, a.lse + li, 512, &q_full[st]);
+        bulk_load(sm + L::LD_OFF + st * 1024 + 512, a.Dv + li, 512, &q_full[st]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_S = idesc_bf16(BKV, BQ, false, false);   // S^T, dP^T: [keys x queries]
+      constexpr uint32_t ID_G = idesc_bf16(BKV, HD, false, true);    // dV, dK: A (TMEM) x B (dO / Q, MN-major)
+      const uint32_t k0 = smem_u32(sm + L::K_OFF), v0 = smem_u32(sm + L::V_OFF);
+      bool ok = mbar_wait(kv_full, 0, a.err);
+      for (int it = 0; it < total && ok && !*abort_flag; ++it) {
+        const int st = it % NS;
+        if (!mbar_wait(&q_full[st], (it / NS) & 1, a.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t q0 = smem_u32(sm + L::Q_OFF + st * L::QT), o0 = smem_u32(sm + L::O_OFF + st * L::QT);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_bf16(t_s, sdesc_sw128(k0 + off, 16, 1024), sdesc_sw128(q0 + off, 16, 1024), ID_S, kk != 0);
+        }
+        umma_commit(s_full);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_bf16(t_dp, sdesc_sw128(v0 + off, 16, 1024), sdesc_sw128(o0 + off, 16, 1024), ID_S, kk != 0);
+        }
+        umma_commit(dp_full);
+        // dV += P^T dO: A = P^T from TMEM (queries 16kk.. at column 64*(kk/4) + 8*(kk%4)),
+        // B = the dO tile read MN-major (16 query rows per step)
+        if (!mbar_wait(pt_full, it & 1, a.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk) {
+          const uint32_t ta = t_s + 64 * (kk >> 2) + 8 * (kk & 3);
+          umma_bf16_ta(t_dv, ta, sdesc_sw128(o0 + kk * 2048, 16384, 1024), ID_G, (it | kk) != 0);
+        }
+        if (!mbar_wait(ds_full, it & 1, a.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk) {
+          const uint32_t ta = t_dp + 64 * (kk >> 2) + 8 * (kk & 3);
+          umma_bf16_ta(t_dk, ta, sdesc_sw128(q0 + kk * 2048, 16384, 1024), ID_G, (it | kk) != 0);
+        }
+        umma_commit(&q_empty[st]);
+        umma_commit(g_done);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    // warps 2-9: thread = key row r; half h = queries [64h, 64h + 64) of every tile
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int c0 = half * 64;
+    const int r = quad * 32 + lane;
+    const int kr = kv0 + r;
+    const uint32_t lo = (uint32_t)(quad * 32) << 16;
+    bool ok = true;
+    for (int it = 0; it < total; ++it) {
+      const int st = it % NS;
+      const int q0 = (kb + it % nqt) * BQ;
+      const bool diag = (it % nqt) == 0;  // the first query tile of each head sits on the diagonal
+      if (*abort_flag || !mbar_wait(s_full, it & 1, a.err) || !mbar_wait(&q_full[st], (it / NS) & 1, a.err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float* Ls = reinterpret_cast<const float*>(sm + L::LD_OFF + st * 1024) + c0;
+      const float* Ds = Ls + 128;
+      uint32_t sr[2][32];
+      tmem_ld32_async(t_s + lo + c0, sr[0]);
+      tmem_ld32_async(t_s + lo + c0 + 32, sr[1]);
+      tmem_wait_ld();
+      tmem_regs(sr[0]);
+      tmem_regs(sr[1]);
+      float p[64];
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float xe = fmaf(__uint_as_float(sr[c >> 5][c & 31]), a.scale_log2, Ls[c] * -LOG2E);
+        float v = (c & 6) == 6 ? exp2_fma(xe) : ex2_approx(xe);
+        if (diag && q0 + c0 + c < kr) v = 0.f;
+        p[c] = v;
+      }
+      uint32_t pk[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) pk[c] = pack_bf16x2(p[2 * c], p[2 * c + 1]);
+      tmem_st32u(t_s + lo + c0, pk);  // P^T over this thread's own S^T columns
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
+      mbar_arrive(pt_full);
+      if (!mbar_wait(dp_full, it & 1, a.err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t dr[2][32];
+      tmem_ld32_async(t_dp + lo + c0, dr[0]);
+      tmem_ld32_async(t_dp + lo + c0 + 32, dr[1]);
+      tmem_wait_ld();
+      tmem_regs(dr[0]);
+      tmem_regs(dr[1]);
+#pragma unroll
+      for (int c = 0; c < 32; ++c)
+        pk[c] = pack_bf16x2(p[2 * c] * (__uint_as_float(dr[(2 * c) >> 5][(2 * c) & 31]) - Ds[2 * c]),
+                            p[2 * c + 1] * (__uint_as_float(dr[(2 * c + 1) >> 5][(2 * c + 1) & 31]) - Ds[2 * c + 1]));
+      tmem_st32u(t_dp + lo + c0, pk);  // dS^T over this thread's own dP^T columns
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
+      mbar_arrive(ds_full);
+    }
+    if (ok && total > 0 && mbar_wait(g_done, (total - 1) & 1, a.err)) {
+      tc_fence_after();
+      const long ld = (long)(a.nq + 2 * a.nkv) * HD;
+      __nv_bfloat16* gk = a.dqkv + ((long)row0 + kr) * ld + (a.nq + hk) * HD;
+      __nv_bfloat16* gv = a.dqkv + ((long)row0 + kr) * ld + (a.nq + a.nkv + hk) * HD;
+#pragma unroll 1
+      for (int c = half * (HD / 2); c < (half + 1) * (HD / 2); c += 32) {
+        float dk[32], dv[32];
+        tmem_ld32(t_dk + lo + c, dk);
+        tmem_ld32(t_dv + lo + c, dv);
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 wk, wv;
+          wk.x = pack_bf16x2(dk[i] * a.scale, dk[i + 1] * a.scale);
+          wk.y = pack_bf16x2(dk[i + 2] * a.scale, dk[i + 3] * a.scale);
+          wk.z = pack_bf16x2(dk[i + 4] * a.scale, dk[i + 5] * a.scale);
+          wk.w = pack_bf16x2(dk[i + 6] * a.scale, dk[i + 7] * a.scale);
+          wv.x = pack_bf16x2(dv[i], dv[i + 1]);
+          wv.y = pack_bf16x2(dv[i + 2], dv[i + 3]);
+          wv.z = pack_bf16x2(dv[i + 4], dv[i + 5]);
+          wv.w = pack_bf16x2(dv[i + 6], dv[i + 7]);
+          *reinterpret_cast<uint4*>(gk + c + i) = wk;
+          *reinterpret_cast<uint4*>(gv + c + i) = wv;
+        }
+      }
+    } else {
+      *abort_flag = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
 // ============================================================== dQ
 template <int HD, int STAGES = 4>
 struct SmQ {
@@ -902,7 +1186,22 @@ void bwd_tc_launch(const torch::Tensor& qkv, const torch::Tensor& dO, const floa
   BwdArgs args{lse, Dv, reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), S, nq, nkv, scale, scale * LOG2E,
                dtb_error_word(), trace_on ? reinterpret_cast<long long*>(trace.data_ptr<int64_t>()) : nullptr};
   auto st = at::cuda::getCurrentCUDAStream();
-  attn_bwd_dkdv_tc_kernel<HD><<<dim3(S / 128, nkv, B), 320, SmKV<HD>::TOTAL, st>>>(kv128, q64, do64, args);
+  // dK/dV: 128-query tiles with P^T / dS^T in TMEM unless DTB_ATTN_DKDV_TM=0
+  static const bool dkdv_tm = [] {
+    const char* e = getenv("DTB_ATTN_DKDV_TM");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  if (dkdv_tm) {
+    static bool cfg_tm = false;
+    if (!cfg_tm) {
+      DTB_CUDA(cudaFuncSetAttribute(attn_bwd_dkdv_tm_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    SmKVT<HD>::TOTAL));
+      cfg_tm = true;
+    }
+    attn_bwd_dkdv_tm_kernel<HD><<<dim3(S / 128, nkv, B), 320, SmKVT<HD>::TOTAL, st>>>(kv128, kv128, do128, args);
+  } else {
+    attn_bwd_dkdv_tc_kernel<HD><<<dim3(S / 128, nkv, B), 320, SmKV<HD>::TOTAL, st>>>(kv128, q64, do64, args);
+  }
   DTB_LAUNCH_CHECK();
   if (dq128)
     attn_bwd_dq128_tc_kernel<HD><<<dim3(S / 128, nq, B), 320, SmQ128<HD>::TOTAL, st>>>(kv128, do128, kv128, args);

@@ -438,7 +438,7 @@ struct SmemPP {
 };
 
 template <int HD>
-__global__ void __maxnreg__(200)
+__global__ void __maxnreg__(192)
     attn_fwd_pp_kernel(const __grid_constant__ CUtensorMap tm_qk, const __grid_constant__ CUtensorMap tm_v,
                        const FwdArgs a) {
   using L = SmemPP<HD>;

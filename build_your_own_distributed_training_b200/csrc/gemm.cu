@@ -95,6 +95,7 @@ struct GemmArgs {
   int ksplit;
   int* sk_flags;
   uint32_t sk_epoch;
+  int d_v8;               // fp32 D: base 32-byte aligned and ldd % 8 == 0 (256-bit stores)
   // AG (all-gather fused in front of the GEMM, sequence parallelism): A is the
   // gathered [M, K] buffer `ag_out`, filled by the kernel's copier warps from this
   // rank's rows `ag_local` and the peers' staged rows (peer_base[p] + stage_off)
@@ -141,7 +142,17 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, int row, int col,
   }
   if (EPI == EPI_STORE_F32 || EPI == EPI_ACC_F32) {
     float* p = reinterpret_cast<float*>(a.D) + (long)row * a.ldd + col;
-    if (ncols_valid >= 32) {
+    if (ncols_valid >= 32 && a.d_v8) {
+      if (EPI == EPI_ACC_F32) {
+        float c[32];
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) ld_global_v8f(p + i, c + i);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] += c[i];
+      }
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) st_global_v8f(p + i, v + i);
+    } else if (ncols_valid >= 32) {
 #pragma unroll
       for (int i = 0; i < 32; i += 4) {
         float4 o = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
@@ -388,6 +399,46 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
           }
         }
       }
+    }
+    return;
+  }
+  if (EPI == EPI_RESIDUAL) {
+    // residual rows are loaded before each TMEM read, so the global-load and
+    // TMEM latencies overlap instead of adding up
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      if (n0 + c >= a.N) break;
+      const int nv = min(32, a.N - (n0 + c));
+      uint4 q[4];
+      const bool vec = row_ok && nv >= 32;
+      if (vec) {
+        const uint4* rp = reinterpret_cast<const uint4*>(a.R + (long)row * a.ldr + n0 + c);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) q[i] = __ldg(rp + i);
+      }
+      float v[32];
+      tmem_ld32(trow + c, v);
+      if (!row_ok) continue;
+      if (!vec) {
+        store_chunk<EPI_RESIDUAL>(a, row, n0 + c, v, nv);
+        continue;
+      }
+      if (a.alpha != nullptr) {
+        const float sc = *a.alpha;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] *= sc;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t* u = &q[i].x;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = unpack_bf16x2(u[k]);
+          v[8 * i + 2 * k] += f.x;
+          v[8 * i + 2 * k + 1] += f.y;
+        }
+      }
+      store_bf16_32(reinterpret_cast<__nv_bfloat16*>(a.D) + (long)row * a.ldd + n0 + c, v);
     }
     return;
   }
@@ -1305,6 +1356,7 @@ static void gemm_impl(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_
   int e = (int)epi;
   if (e == EPI_STORE_BF16 && f32out) e = EPI_STORE_F32;
   if (e == EPI_ACC_F32) TORCH_CHECK(f32out, "gemm: accumulate epilogue needs an fp32 output");
+  g.d_v8 = f32out && (reinterpret_cast<uintptr_t>(D.data_ptr()) & 31) == 0 && D.stride(0) % 8 == 0;
   if (e == EPI_STORE_BF16 || e == EPI_RESIDUAL || e == EPI_ROPE || e == EPI_SWIGLU || e == EPI_PEER_AR ||
       e == EPI_CE_GRAD || e == EPI_ACC_BF16OUT)
     TORCH_CHECK(D.scalar_type() == at::kBFloat16, "gemm: bf16 output expected");
