@@ -420,6 +420,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 //              tile B.  P_X goes to one bf16 shared buffer per tile; the
 //              softmax of tile X at step j writes it once PV_X(j-1) has read it.
 // Tile A = 2*pair, tile B = 2*pair + 1: B has one more key tile (its diagonal).
+// Registers: a 10-warp block is allocated registers as 12 warps (warpgroup
+// granularity), so the cap is 168 per thread, not 65536 / 320; a larger cap
+// compiles but fails to launch.
 // Same online softmax as attn_fwd_tc_kernel (exp2 form, stale-max rescale).
 template <int HD>
 struct SmemPP {
@@ -438,7 +441,7 @@ struct SmemPP {
 };
 
 template <int HD>
-__global__ void __maxnreg__(192)
+__global__ void __launch_bounds__(320, 1)
     attn_fwd_pp_kernel(const __grid_constant__ CUtensorMap tm_qk, const __grid_constant__ CUtensorMap tm_v,
                        const FwdArgs a) {
   using L = SmemPP<HD>;
