@@ -122,6 +122,47 @@ def case_gemm_peer_rs():
     return run, 2 * T * D * (D // 2), 0
 
 
+def case_gemm_peer_ar_two_shot():
+    # tp=4 two-shot all-reduce epilogue, rank 0 with three emulated partners: [T, D/4] x [D, D/4]^T
+    ranks = 4
+    a, b, r = _bf(T, D // ranks), _bf(D, D // ranks), _bf(T, D)
+    out = torch.empty(T, D, device=DEV, dtype=BF)
+    stage = T * D * 2
+    flag_off = (stage + 255) // 256 * 256
+    nflags = 2 * (T // 128 + 2) * (D // 128 + 2) * 4
+    heaps, bases = _emulated_heaps(ranks, flag_off + (ranks + 1) * nflags * 4)
+    for p in range(1, ranks):
+        heaps[p][:stage].view(BF).copy_(_bf(T * D))  # partials (read for rank 0's own units) / sums (copied)
+    epoch = [0]
+
+    def run():
+        epoch[0] += 1
+        heaps[0][flag_off:].view(torch.int32).fill_(epoch[0])    # partners' partial and done flags
+        native().gemm_peer_ar(a, b, out, False, r, None, bases, 0, 0, flag_off, epoch[0], 1.0, two_shot=True)
+    return run, 2 * T * D * (D // ranks), 0
+
+
+def case_gemm_all_gather():
+    # tp=2 sequence-parallel QKV input: rank 0 gathers [T, D] (its 4096 rows + the emulated
+    # partner's staged rows) inside the GEMM, then [T, D] x [3D/2, D]^T
+    ranks, R = 2, T // 2
+    x_local = _bf(R, D)
+    w = _bf(3 * D // 2, D)
+    stage = R * D * 2
+    staged_off = (stage + 255) // 256 * 256
+    heaps, bases = _emulated_heaps(ranks, staged_off + 256)
+    heaps[1][:stage].view(BF).copy_(_bf(R * D))
+    xg = torch.empty(T, D, device=DEV, dtype=BF)
+    out = torch.empty(T, 3 * D // 2, device=DEV, dtype=BF)
+    epoch = [0]
+
+    def run():
+        epoch[0] += 1
+        heaps[0][staged_off:staged_off + 4 * ranks].view(torch.int32).fill_(epoch[0])
+        native().gemm_ag(xg, x_local, w, out, 0, None, None, None, 0, 0, bases, 0, 0, staged_off, epoch[0], 1.0)
+    return run, 2 * T * D * (3 * D // 2), 0
+
+
 def case_peer_all_gather():
     shard = 128 << 20
     heaps, bases = _emulated_heaps(2, shard)
