@@ -111,6 +111,9 @@ struct GemmArgs {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
+// ring depth when a stage is 32 KB per CTA (CTA pairs, or 128-column tiles):
+// 7 x 32 KB + barriers fits the 227 KB a CTA may use
+constexpr int kStages32K = 7;
 constexpr int GROUP_M = 16;
 
 __device__ __forceinline__ void tile_coords(int tile, int mblocks, int nblocks, int& mb, int& nb) {
@@ -1166,7 +1169,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cu
 template <int BN, bool A_MN, bool B_MN, bool PAIR>
 static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t st) {
   // per-CTA stage: 16 KB of A + 32 KB (BN=256), 16 KB (BN=128 or a pair's half of 256) of B
-  constexpr int ST = (BN == 256 && !PAIR) ? 4 : 6;
+  constexpr int ST = (BN == 256 && !PAIR) ? 4 : kStages32K;
   switch (epi) {
     case EPI_STORE_BF16: launch<BN, ST, A_MN, B_MN, EPI_STORE_BF16, PAIR>(ta, tb, g, st); break;
     case EPI_STORE_F32: launch<BN, ST, A_MN, B_MN, EPI_STORE_F32, PAIR>(ta, tb, g, st); break;
@@ -1200,7 +1203,7 @@ static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, 
 // layers use)
 template <int BN, bool PAIR>
 static void dispatch_epi_ag(int epi, const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t st) {
-  constexpr int ST = (BN == 256 && !PAIR) ? 4 : 6;
+  constexpr int ST = (BN == 256 && !PAIR) ? 4 : kStages32K;
   switch (epi) {
     case EPI_STORE_BF16: launch<BN, ST, false, false, EPI_STORE_BF16, PAIR, true>(ta, tb, g, st); break;
     case EPI_ROPE: launch<BN, ST, false, false, EPI_ROPE, PAIR, true>(ta, tb, g, st); break;

@@ -443,6 +443,11 @@ class TPComm:
     # standalone collectives on bf16 activations
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         x = x.contiguous()
+        if self.two_shot and x.dim() >= 2 and x.shape[0] % self.size == 0 \
+                and (x.numel() // x.shape[0]) % 8 == 0:
+            # two-shot: each rank sums its row block from every peer, then every rank
+            # pulls every block (2(tp-1)/tp payloads in, against tp-1 one-shot)
+            return self.all_gather_rows(self.reduce_scatter_rows(x))
         off = self._slot()
         self._staging(off, tuple(x.shape)).copy_(x)
         self.barrier()
