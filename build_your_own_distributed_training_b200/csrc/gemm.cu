@@ -112,8 +112,8 @@ struct GemmArgs {
 constexpr int BM = 128;
 constexpr int BK = 64;
 // ring depth when a stage is 32 KB per CTA (CTA pairs, or 128-column tiles):
-// 7 x 32 KB + barriers fits the 227 KB a CTA may use
-constexpr int kStages32K = 7;
+// (7 stages measured no faster: 1256 vs 1267 TFLOP/s at 4096^3, so 6 leave room)
+constexpr int kStages32K = 6;
 constexpr int GROUP_M = 16;
 
 __device__ __forceinline__ void tile_coords(int tile, int mblocks, int nblocks, int& mb, int& nb) {
@@ -126,13 +126,17 @@ __device__ __forceinline__ void tile_coords(int tile, int mblocks, int nblocks, 
   nb = r / gm;
 }
 
-template <int BN, int STAGES, bool PAIR = false>
+// TSTORE: 4 KB of shared memory per epilogue warp for the TMA-store epilogue
+template <int BN, int STAGES, bool PAIR = false, bool TSTORE = false>
 struct SmemLayout {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;  // a CTA pair splits B by columns
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int STG_OFF = STAGES * STAGE_BYTES;
+  static constexpr int STG_BYTES = TSTORE ? 8 * 4096 : 0;
+  static constexpr int BAR_OFF = STG_OFF + STG_BYTES;
   static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 4) * 8 + 16 + 1024;  // + alignment slack
+  static_assert(TOTAL <= 232448, "shared memory per CTA");
 };
 
 // ---------------------------------------------------------------- epilogue
@@ -451,6 +455,65 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
     float v[32];
     tmem_ld32(trow + c, v);
     if (row_ok) store_chunk<EPI>(a, row, n0 + c, v, min(32, a.N - (n0 + c)));
+  }
+}
+
+// ---------------------------------------------------------------- TMA-store epilogue (bf16 D)
+// Each epilogue warp converts 32 rows x 64 columns of its accumulator rows to
+// bf16, writes them into its 4 KB staging slot in the 128-byte-swizzled layout
+// of the D tensor map's [32 x 64] box, and one lane issues a bulk tensor store.
+// The global writes then go out as whole 128-byte lines from the TMA unit
+// instead of one 16-byte piece per thread and row from the load/store unit
+// (measured: the row-per-thread stores held the tensor pipe at ~77% busy where
+// an epilogue without stores reached ~91%).  Rows past M are clipped by the
+// tensor map; before a slot is rewritten its previous store must have read it.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(m),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+template <int BN>
+__device__ __forceinline__ void epilogue_tma_store(const GemmArgs& a, const CUtensorMap* tmD, uint8_t* stg,
+                                                   uint32_t tbase, int mb, int nb, int quad, int lane) {
+  const uint32_t trow = tbase + ((uint32_t)(quad * 32) << 16);
+  const int n0 = nb * BN;
+  const int grow0 = mb * BM + quad * 32;
+  const float sc = a.alpha != nullptr ? *a.alpha : 1.f;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 64) {
+    if (n0 + c >= a.N) break;
+    uint32_t r1[32], r2[32];
+    tmem_ld32_async(trow + c, r1);
+    tmem_ld32_async(trow + c + 32, r2);
+    tmem_wait_ld();
+    tmem_regs(r1);
+    tmem_regs(r2);
+    uint32_t pk[32];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      pk[i] = pack_bf16x2(__uint_as_float(r1[2 * i]) * sc, __uint_as_float(r1[2 * i + 1]) * sc);
+      pk[16 + i] = pack_bf16x2(__uint_as_float(r2[2 * i]) * sc, __uint_as_float(r2[2 * i + 1]) * sc);
+    }
+    // the slot's previous store has read it
+    if (lane == 0) bulk_wait_group_read0();
+    __syncwarp();
+    uint8_t* rowp = stg + lane * 128;
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc)
+      *reinterpret_cast<uint4*>(rowp + ((cc ^ (lane & 7)) << 4)) =
+          make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmD, stg, n0 + c, grow0);
+      bulk_commit_group();
+    }
   }
 }
 
@@ -819,10 +882,11 @@ __device__ __forceinline__ bool ag_wait_rows(const GemmArgs& a, int row0, int ro
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool PAIR, bool AG = false>
 __global__ void __launch_bounds__(AG ? 384 : 320, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const GemmArgs args) {
+                        const __grid_constant__ CUtensorMap tmD, const GemmArgs args) {
   static_assert(!AG || (!A_MN && !B_MN), "all-gather mode gathers K-major A rows");
   static_assert(!PAIR || BN == 256, "CTA pairs use 256-column tiles");
-  using L = SmemLayout<BN, STAGES, PAIR>;
+  constexpr bool TSTORE = EPI == EPI_STORE_BF16;
+  using L = SmemLayout<BN, STAGES, PAIR, TSTORE>;
   constexpr int TILE_M = PAIR ? 2 * BM : BM;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1019,6 +1083,9 @@ __global__ void __launch_bounds__(AG ? 384 : 320, 1)
       tc_fence_after();
       if constexpr (EPI == EPI_PEER_AR) {
         peer_ar_stage<BN>(args, tmem_base + acc * BN, slab, nb, quad, lane);
+      } else if constexpr (TSTORE) {
+        epilogue_tma_store<BN>(args, &tmD, smem + L::STG_OFF + (warp - 2) * 4096, tmem_base + acc * BN, slab, nb,
+                               quad, lane);
       } else if constexpr (EPI == EPI_STORE_F32 || EPI == EPI_ACC_F32) {
         if (split == 0) {
           epilogue_tile<BN, EPI>(args, tmem_base + acc * BN, slab, nb, quad, lane);
@@ -1079,6 +1146,10 @@ __global__ void __launch_bounds__(AG ? 384 : 320, 1)
         *abort_flag = 1;
       }
     }
+    if constexpr (TSTORE) {
+      if (lane == 0) bulk_wait_group0();  // this warp's stores are done before its staging slot goes away
+      __syncwarp();
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -1132,8 +1203,9 @@ static CUtensorMap make_map(const void* base, long inner, long rows, long row_st
 static int num_sms() { return device_sm_count(); }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool PAIR, bool AG = false>
-static void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t st) {
-  using L = SmemLayout<BN, STAGES, PAIR>;
+static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, GemmArgs& g,
+                   cudaStream_t st) {
+  using L = SmemLayout<BN, STAGES, PAIR, EPI == EPI_STORE_BF16>;
   auto kern = gemm_tcgen05_kernel<BN, STAGES, A_MN, B_MN, EPI, PAIR, AG>;
   constexpr int NT = AG ? 384 : 320;
   static bool configured = false;
@@ -1158,42 +1230,43 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cu
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    DTB_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, g));
+    DTB_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, td, g));
   } else {
     const int grid = std::min(work, num_sms());
-    kern<<<grid, NT, L::TOTAL, st>>>(ta, tb, g);
+    kern<<<grid, NT, L::TOTAL, st>>>(ta, tb, td, g);
   }
   DTB_LAUNCH_CHECK();
 }
 
 template <int BN, bool A_MN, bool B_MN, bool PAIR>
-static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t st) {
+static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, GemmArgs& g,
+                         cudaStream_t st) {
   // per-CTA stage: 16 KB of A + 32 KB (BN=256), 16 KB (BN=128 or a pair's half of 256) of B
   constexpr int ST = (BN == 256 && !PAIR) ? 4 : kStages32K;
   switch (epi) {
-    case EPI_STORE_BF16: launch<BN, ST, A_MN, B_MN, EPI_STORE_BF16, PAIR>(ta, tb, g, st); break;
-    case EPI_STORE_F32: launch<BN, ST, A_MN, B_MN, EPI_STORE_F32, PAIR>(ta, tb, g, st); break;
-    case EPI_ACC_F32: launch<BN, ST, A_MN, B_MN, EPI_ACC_F32, PAIR>(ta, tb, g, st); break;
+    case EPI_STORE_BF16: launch<BN, ST, A_MN, B_MN, EPI_STORE_BF16, PAIR>(ta, tb, td, g, st); break;
+    case EPI_STORE_F32: launch<BN, ST, A_MN, B_MN, EPI_STORE_F32, PAIR>(ta, tb, td, g, st); break;
+    case EPI_ACC_F32: launch<BN, ST, A_MN, B_MN, EPI_ACC_F32, PAIR>(ta, tb, td, g, st); break;
     case EPI_RESIDUAL:
-      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_RESIDUAL, PAIR>(ta, tb, g, st); break; }
+      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_RESIDUAL, PAIR>(ta, tb, td, g, st); break; }
       TORCH_CHECK(false, "residual epilogue needs K-major operands");
     case EPI_ROPE:
-      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_ROPE, PAIR>(ta, tb, g, st); break; }
+      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_ROPE, PAIR>(ta, tb, td, g, st); break; }
       TORCH_CHECK(false, "rope epilogue needs K-major operands");
     case EPI_SWIGLU:
-      if constexpr (!A_MN && !B_MN && BN == 256) { launch<BN, ST, A_MN, B_MN, EPI_SWIGLU, PAIR>(ta, tb, g, st); break; }
+      if constexpr (!A_MN && !B_MN && BN == 256) { launch<BN, ST, A_MN, B_MN, EPI_SWIGLU, PAIR>(ta, tb, td, g, st); break; }
       TORCH_CHECK(false, "swiglu epilogue needs K-major operands and BN=256");
     case EPI_PEER_AR:
-      if constexpr (!A_MN) { launch<BN, ST, A_MN, B_MN, EPI_PEER_AR, PAIR>(ta, tb, g, st); break; }
+      if constexpr (!A_MN) { launch<BN, ST, A_MN, B_MN, EPI_PEER_AR, PAIR>(ta, tb, td, g, st); break; }
       TORCH_CHECK(false, "peer all-reduce epilogue needs a K-major A operand");
     case EPI_CE_STATS:
-      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_CE_STATS, PAIR>(ta, tb, g, st); break; }
+      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_CE_STATS, PAIR>(ta, tb, td, g, st); break; }
       TORCH_CHECK(false, "cross-entropy epilogues need K-major operands");
     case EPI_CE_GRAD:
-      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_CE_GRAD, PAIR>(ta, tb, g, st); break; }
+      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_CE_GRAD, PAIR>(ta, tb, td, g, st); break; }
       TORCH_CHECK(false, "cross-entropy epilogues need K-major operands");
     case EPI_ACC_BF16OUT:
-      if constexpr (!A_MN && B_MN) { launch<BN, ST, A_MN, B_MN, EPI_ACC_BF16OUT, PAIR>(ta, tb, g, st); break; }
+      if constexpr (!A_MN && B_MN) { launch<BN, ST, A_MN, B_MN, EPI_ACC_BF16OUT, PAIR>(ta, tb, td, g, st); break; }
       TORCH_CHECK(false, "fp32-accumulator epilogue is built for the input-gradient layout (A K-major, B MN-major)");
     default: DTB_CHECK(false, "unknown epilogue %d", epi);
   }
@@ -1202,13 +1275,14 @@ static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, 
 // all-gather -> GEMM launches (K-major operands; the epilogues the column-parallel
 // layers use)
 template <int BN, bool PAIR>
-static void dispatch_epi_ag(int epi, const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t st) {
+static void dispatch_epi_ag(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
+                            GemmArgs& g, cudaStream_t st) {
   constexpr int ST = (BN == 256 && !PAIR) ? 4 : kStages32K;
   switch (epi) {
-    case EPI_STORE_BF16: launch<BN, ST, false, false, EPI_STORE_BF16, PAIR, true>(ta, tb, g, st); break;
-    case EPI_ROPE: launch<BN, ST, false, false, EPI_ROPE, PAIR, true>(ta, tb, g, st); break;
+    case EPI_STORE_BF16: launch<BN, ST, false, false, EPI_STORE_BF16, PAIR, true>(ta, tb, td, g, st); break;
+    case EPI_ROPE: launch<BN, ST, false, false, EPI_ROPE, PAIR, true>(ta, tb, td, g, st); break;
     case EPI_SWIGLU:
-      if constexpr (BN == 256) { launch<BN, ST, false, false, EPI_SWIGLU, PAIR, true>(ta, tb, g, st); break; }
+      if constexpr (BN == 256) { launch<BN, ST, false, false, EPI_SWIGLU, PAIR, true>(ta, tb, td, g, st); break; }
       TORCH_CHECK(false, "swiglu epilogue needs BN=256");
     default: DTB_CHECK(false, "all-gather GEMM: epilogue %d not built", epi);
   }
@@ -1477,27 +1551,29 @@ static void gemm_impl(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_
             (int)a_mn, (int)b_mn, e, BN, A.data_ptr(), B.data_ptr(), D.data_ptr(), (const void*)g.alpha);
   const CUtensorMap ta = a_mn ? make_map(A.data_ptr(), M, K, A.stride(0), BK) : make_map(A.data_ptr(), K, M, A.stride(0), BM);
   const CUtensorMap tb = b_mn ? make_map(B.data_ptr(), NB, K, B.stride(0), BK) : make_map(B.data_ptr(), K, NB, B.stride(0), 128);
+  // bf16 store epilogue: D through [32 rows x 64 columns] TMA stores (other epilogues ignore td)
+  const CUtensorMap td = e == EPI_STORE_BF16 ? make_map(D.data_ptr(), g.N, D.size(0), D.stride(0), 32) : ta;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (ag != nullptr) {
-    if (BN == 256 && pair) dispatch_epi_ag<256, true>(e, ta, tb, g, st);
-    else if (BN == 256) dispatch_epi_ag<256, false>(e, ta, tb, g, st);
-    else dispatch_epi_ag<128, false>(e, ta, tb, g, st);
+    if (BN == 256 && pair) dispatch_epi_ag<256, true>(e, ta, tb, td, g, st);
+    else if (BN == 256) dispatch_epi_ag<256, false>(e, ta, tb, td, g, st);
+    else dispatch_epi_ag<128, false>(e, ta, tb, td, g, st);
     return;
   }
   if (BN == 256 && pair) {
-    if (!a_mn && !b_mn) dispatch_epi<256, false, false, true>(e, ta, tb, g, st);
-    else if (!a_mn && b_mn) dispatch_epi<256, false, true, true>(e, ta, tb, g, st);
-    else if (a_mn && b_mn) dispatch_epi<256, true, true, true>(e, ta, tb, g, st);
+    if (!a_mn && !b_mn) dispatch_epi<256, false, false, true>(e, ta, tb, td, g, st);
+    else if (!a_mn && b_mn) dispatch_epi<256, false, true, true>(e, ta, tb, td, g, st);
+    else if (a_mn && b_mn) dispatch_epi<256, true, true, true>(e, ta, tb, td, g, st);
     else TORCH_CHECK(false, "gemm: layout (MN, K) not built");
   } else if (BN == 256) {
-    if (!a_mn && !b_mn) dispatch_epi<256, false, false, false>(e, ta, tb, g, st);
-    else if (!a_mn && b_mn) dispatch_epi<256, false, true, false>(e, ta, tb, g, st);
-    else if (a_mn && b_mn) dispatch_epi<256, true, true, false>(e, ta, tb, g, st);
+    if (!a_mn && !b_mn) dispatch_epi<256, false, false, false>(e, ta, tb, td, g, st);
+    else if (!a_mn && b_mn) dispatch_epi<256, false, true, false>(e, ta, tb, td, g, st);
+    else if (a_mn && b_mn) dispatch_epi<256, true, true, false>(e, ta, tb, td, g, st);
     else TORCH_CHECK(false, "gemm: layout (MN, K) not built");
   } else {
-    if (!a_mn && !b_mn) dispatch_epi<128, false, false, false>(e, ta, tb, g, st);
-    else if (!a_mn && b_mn) dispatch_epi<128, false, true, false>(e, ta, tb, g, st);
-    else if (a_mn && b_mn) dispatch_epi<128, true, true, false>(e, ta, tb, g, st);
+    if (!a_mn && !b_mn) dispatch_epi<128, false, false, false>(e, ta, tb, td, g, st);
+    else if (!a_mn && b_mn) dispatch_epi<128, false, true, false>(e, ta, tb, td, g, st);
+    else if (a_mn && b_mn) dispatch_epi<128, true, true, false>(e, ta, tb, td, g, st);
     else TORCH_CHECK(false, "gemm: layout (MN, K) not built");
   }
 }
