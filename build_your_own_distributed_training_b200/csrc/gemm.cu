@@ -96,6 +96,7 @@ struct GemmArgs {
   int* sk_flags;
   uint32_t sk_epoch;
   int d_v8;               // fp32 D: base 32-byte aligned and ldd % 8 == 0 (256-bit stores)
+  int d_tma;              // store / accumulate / residual epilogues: D (and R) go through tensor maps
   // AG (all-gather fused in front of the GEMM, sequence parallelism): A is the
   // gathered [M, K] buffer `ag_out`, filled by the kernel's copier warps from this
   // rank's rows `ag_local` and the peers' staged rows (peer_base[p] + stage_off)
@@ -126,7 +127,12 @@ __device__ __forceinline__ void tile_coords(int tile, int mblocks, int nblocks, 
   nb = r / gm;
 }
 
-// TSTORE: 4 KB of shared memory per epilogue warp for the TMA-store epilogue
+// epilogues whose output leaves through TMA bulk stores (when args.d_tma is set)
+__host__ __device__ constexpr bool tma_store_epi(int epi) {
+  return epi == EPI_STORE_BF16 || epi == EPI_STORE_F32 || epi == EPI_ACC_F32 || epi == EPI_RESIDUAL;
+}
+
+// TSTORE: 4 KB of shared memory per epilogue warp for the TMA-store epilogues
 template <int BN, int STAGES, bool PAIR = false, bool TSTORE = false>
 struct SmemLayout {
   static constexpr int A_BYTES = BM * BK * 2;
@@ -135,7 +141,8 @@ struct SmemLayout {
   static constexpr int STG_OFF = STAGES * STAGE_BYTES;
   static constexpr int STG_BYTES = TSTORE ? 8 * 4096 : 0;
   static constexpr int BAR_OFF = STG_OFF + STG_BYTES;
-  static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 4) * 8 + 16 + 1024;  // + alignment slack
+  static constexpr int RBAR_OFF = BAR_OFF + (2 * STAGES + 4) * 8 + 16;  // TSTORE: one barrier per epilogue warp
+  static constexpr int TOTAL = RBAR_OFF + (TSTORE ? 8 * 8 : 0) + 1024;   // + alignment slack
   static_assert(TOTAL <= 232448, "shared memory per CTA");
 };
 
@@ -433,7 +440,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
       if (a.alpha != nullptr) {
         const float sc = *a.alpha;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] *= sc;
+        for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(v[i], sc);
       }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -441,8 +448,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const float2 f = unpack_bf16x2(u[k]);
-          v[8 * i + 2 * k] += f.x;
-          v[8 * i + 2 * k + 1] += f.y;
+          v[8 * i + 2 * k] = __fadd_rn(v[8 * i + 2 * k], f.x);
+          v[8 * i + 2 * k + 1] = __fadd_rn(v[8 * i + 2 * k + 1], f.y);
         }
       }
       store_bf16_32(reinterpret_cast<__nv_bfloat16*>(a.D) + (long)row * a.ldd + n0 + c, v);
@@ -508,6 +515,114 @@ __device__ __forceinline__ void epilogue_tma_store(const GemmArgs& a, const CUte
     for (int cc = 0; cc < 8; ++cc)
       *reinterpret_cast<uint4*>(rowp + ((cc ^ (lane & 7)) << 4)) =
           make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmD, stg, n0 + c, grow0);
+      bulk_commit_group();
+    }
+  }
+}
+
+// fp32 D: a [32 rows x 32 columns] box (128 bytes per row) per store.  With
+// ACC the box is added to D by the TMA unit (cp.reduce.async.bulk.tensor .add):
+// the weight-gradient accumulation never reads D into the SM.  Each element is
+// added once per launch, in the same fp32 operation as a load-add-store, so the
+// result is the same bits.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* m, const void* src, int c0, int c1) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(m),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+
+template <int BN, bool ACC>
+__device__ __forceinline__ void epilogue_tma_f32(const GemmArgs& a, const CUtensorMap* tmD, uint8_t* stg,
+                                                 uint32_t tbase, int mb, int nb, int quad, int lane) {
+  const uint32_t trow = tbase + ((uint32_t)(quad * 32) << 16);
+  const int n0 = nb * BN;
+  const int grow0 = mb * BM + quad * 32;
+  const float sc = a.alpha != nullptr ? *a.alpha : 1.f;
+  uint32_t r[32];
+  if (n0 < a.N) tmem_ld32_async(trow, r);
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    if (n0 + c >= a.N) break;
+    tmem_wait_ld();
+    tmem_regs(r);
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * sc;
+    // next chunk's TMEM read overlaps this chunk's staging
+    if (c + 32 < BN && n0 + c + 32 < a.N) tmem_ld32_async(trow + c + 32, r);
+    if (lane == 0) bulk_wait_group_read0();
+    __syncwarp();
+    uint8_t* rowp = stg + lane * 128;
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc)
+      *reinterpret_cast<float4*>(rowp + ((cc ^ (lane & 7)) << 4)) =
+          make_float4(v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if constexpr (ACC) tma_reduce_add_2d(tmD, stg, n0 + c, grow0);
+      else tma_store_2d(tmD, stg, n0 + c, grow0);
+      bulk_commit_group();
+    }
+  }
+}
+
+// D = alpha * acc + R (bf16): the residual's [32 x 64] box is brought into the
+// staging slot by TMA (issued before the accumulator is read, so both latencies
+// overlap), summed in place and stored from the same slot.  `rbar` is this
+// warp's barrier, `rphase` its phase.
+template <int BN>
+__device__ __forceinline__ void epilogue_tma_residual(const GemmArgs& a, const CUtensorMap* tmD,
+                                                      const CUtensorMap* tmR, uint8_t* stg, uint64_t* rbar,
+                                                      uint32_t& rphase, uint32_t tbase, int mb, int nb, int quad,
+                                                      int lane, volatile int* abort_flag) {
+  const uint32_t trow = tbase + ((uint32_t)(quad * 32) << 16);
+  const int n0 = nb * BN;
+  const int grow0 = mb * BM + quad * 32;
+  const float sc = a.alpha != nullptr ? *a.alpha : 1.f;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 64) {
+    if (n0 + c >= a.N) break;
+    if (lane == 0) {
+      bulk_wait_group_read0();  // the slot's previous store has read it
+      mbar_arrive_expect_tx(rbar, 4096);
+      tma_load_2d(stg, tmR, rbar, n0 + c, grow0);
+    }
+    uint32_t r1[32], r2[32];
+    tmem_ld32_async(trow + c, r1);
+    tmem_ld32_async(trow + c + 32, r2);
+    tmem_wait_ld();
+    tmem_regs(r1);
+    tmem_regs(r2);
+    const bool ok = mbar_wait(rbar, rphase, a.err);
+    rphase ^= 1;
+    if (!ok) {
+      *abort_flag = 1;  // the residual never arrived: leave the tile unwritten, the error word is set
+      return;
+    }
+    uint8_t* rowp = stg + lane * 128;
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc) {
+      uint4* q = reinterpret_cast<uint4*>(rowp + ((cc ^ (lane & 7)) << 4));
+      const uint4 in = *q;
+      const uint32_t* rr = cc < 4 ? r1 : r2;
+      const int b = (cc & 3) * 8;
+      const float2 f0 = unpack_bf16x2(in.x), f1 = unpack_bf16x2(in.y), f2 = unpack_bf16x2(in.z),
+                   f3 = unpack_bf16x2(in.w);
+      uint4 o;
+      // (alpha * acc) + r rounded twice, as in the row-per-thread epilogue
+#define DTB_AR(i, f) __fadd_rn(__fmul_rn(__uint_as_float(rr[b + (i)]), sc), f)
+      o.x = pack_bf16x2(DTB_AR(0, f0.x), DTB_AR(1, f0.y));
+      o.y = pack_bf16x2(DTB_AR(2, f1.x), DTB_AR(3, f1.y));
+      o.z = pack_bf16x2(DTB_AR(4, f2.x), DTB_AR(5, f2.y));
+      o.w = pack_bf16x2(DTB_AR(6, f3.x), DTB_AR(7, f3.y));
+#undef DTB_AR
+      *q = o;
+    }
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
@@ -882,10 +997,11 @@ __device__ __forceinline__ bool ag_wait_rows(const GemmArgs& a, int row0, int ro
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool PAIR, bool AG = false>
 __global__ void __launch_bounds__(AG ? 384 : 320, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmD, const GemmArgs args) {
+                        const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmR,
+                        const GemmArgs args) {
   static_assert(!AG || (!A_MN && !B_MN), "all-gather mode gathers K-major A rows");
   static_assert(!PAIR || BN == 256, "CTA pairs use 256-column tiles");
-  constexpr bool TSTORE = EPI == EPI_STORE_BF16;
+  constexpr bool TSTORE = tma_store_epi(EPI);
   using L = SmemLayout<BN, STAGES, PAIR, TSTORE>;
   constexpr int TILE_M = PAIR ? 2 * BM : BM;
   extern __shared__ uint8_t smem_raw[];
@@ -913,6 +1029,8 @@ __global__ void __launch_bounds__(AG ? 384 : 320, 1)
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], PAIR ? 8 : 4);  // one arrival per epilogue warp of each CTA
     }
+    if constexpr (TSTORE)
+      for (int i = 0; i < 8; ++i) mbar_init(reinterpret_cast<uint64_t*>(smem + L::RBAR_OFF) + i, 1);
     *abort_flag = 0;
     if constexpr (PAIR) fence_mbar_init_cluster();
     else fence_mbar_init();
@@ -1067,6 +1185,7 @@ __global__ void __launch_bounds__(AG ? 384 : 320, 1)
     int t = 0;
     int pend_tile = -1, pend_mb = 0, pend_nb = 0;  // EPI_PEER_AR: tile published, not yet reduced
     int pend2_tile = -1, pend2_mb = 0, pend2_nb = 0;  // two-shot: reduced by its owner, not yet copied
+    uint32_t rphase = 0;                               // TMA residual epilogue: this warp's barrier phase
     for (int u = unit; u < args.num_tiles * args.ksplit; u += units, ++t) {
       const int tile = u % args.num_tiles, split = u / args.num_tiles;
       const int acc = t & 1;
@@ -1083,9 +1202,17 @@ __global__ void __launch_bounds__(AG ? 384 : 320, 1)
       tc_fence_after();
       if constexpr (EPI == EPI_PEER_AR) {
         peer_ar_stage<BN>(args, tmem_base + acc * BN, slab, nb, quad, lane);
-      } else if constexpr (TSTORE) {
-        epilogue_tma_store<BN>(args, &tmD, smem + L::STG_OFF + (warp - 2) * 4096, tmem_base + acc * BN, slab, nb,
-                               quad, lane);
+      } else if (TSTORE && args.d_tma) {
+        uint8_t* stg = smem + L::STG_OFF + (warp - 2) * 4096;
+        const uint32_t tb = tmem_base + acc * BN;
+        if constexpr (EPI == EPI_STORE_BF16) {
+          epilogue_tma_store<BN>(args, &tmD, stg, tb, slab, nb, quad, lane);
+        } else if constexpr (EPI == EPI_RESIDUAL) {
+          epilogue_tma_residual<BN>(args, &tmD, &tmR, stg, reinterpret_cast<uint64_t*>(smem + L::RBAR_OFF) + (warp - 2),
+                                    rphase, tb, slab, nb, quad, lane, abort_flag);
+        } else if constexpr (EPI == EPI_STORE_F32 || EPI == EPI_ACC_F32) {
+          epilogue_tma_f32<BN, EPI == EPI_ACC_F32>(args, &tmD, stg, tb, slab, nb, quad, lane);
+        }
       } else if constexpr (EPI == EPI_STORE_F32 || EPI == EPI_ACC_F32) {
         if (split == 0) {
           epilogue_tile<BN, EPI>(args, tmem_base + acc * BN, slab, nb, quad, lane);
@@ -1200,12 +1327,31 @@ static CUtensorMap make_map(const void* base, long inner, long rows, long row_st
   return m;
 }
 
+// Output / residual map for the TMA-store epilogues: [32 rows x 128 bytes] boxes
+// (64 bf16 or 32 fp32 columns), 128-byte swizzle.  Returns false (the caller then
+// keeps the row-per-thread epilogue) when the base or the row stride is not
+// 16-byte aligned, which a tensor map cannot describe.
+static bool make_out_map(CUtensorMap* m, const void* base, bool f32, long inner, long rows, long row_stride_elems) {
+  const int es = f32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (row_stride_elems * es) % 16 != 0 || inner <= 0 || rows <= 0)
+    return false;
+  bind_context_once();
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(row_stride_elems * es)};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / es), 32};
+  cuuint32_t estr[2] = {1, 1};
+  return encode_fn()(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                     const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 static int num_sms() { return device_sm_count(); }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool PAIR, bool AG = false>
-static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, GemmArgs& g,
+static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const CUtensorMap& tr, GemmArgs& g,
                    cudaStream_t st) {
-  using L = SmemLayout<BN, STAGES, PAIR, EPI == EPI_STORE_BF16>;
+  using L = SmemLayout<BN, STAGES, PAIR, tma_store_epi(EPI)>;
   auto kern = gemm_tcgen05_kernel<BN, STAGES, A_MN, B_MN, EPI, PAIR, AG>;
   constexpr int NT = AG ? 384 : 320;
   static bool configured = false;
@@ -1230,43 +1376,43 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    DTB_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, td, g));
+    DTB_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, td, tr, g));
   } else {
     const int grid = std::min(work, num_sms());
-    kern<<<grid, NT, L::TOTAL, st>>>(ta, tb, td, g);
+    kern<<<grid, NT, L::TOTAL, st>>>(ta, tb, td, tr, g);
   }
   DTB_LAUNCH_CHECK();
 }
 
 template <int BN, bool A_MN, bool B_MN, bool PAIR>
-static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, GemmArgs& g,
+static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const CUtensorMap& tr, GemmArgs& g,
                          cudaStream_t st) {
   // per-CTA stage: 16 KB of A + 32 KB (BN=256), 16 KB (BN=128 or a pair's half of 256) of B
   constexpr int ST = (BN == 256 && !PAIR) ? 4 : kStages32K;
   switch (epi) {
-    case EPI_STORE_BF16: launch<BN, ST, A_MN, B_MN, EPI_STORE_BF16, PAIR>(ta, tb, td, g, st); break;
-    case EPI_STORE_F32: launch<BN, ST, A_MN, B_MN, EPI_STORE_F32, PAIR>(ta, tb, td, g, st); break;
-    case EPI_ACC_F32: launch<BN, ST, A_MN, B_MN, EPI_ACC_F32, PAIR>(ta, tb, td, g, st); break;
+    case EPI_STORE_BF16: launch<BN, ST, A_MN, B_MN, EPI_STORE_BF16, PAIR>(ta, tb, td, tr, g, st); break;
+    case EPI_STORE_F32: launch<BN, ST, A_MN, B_MN, EPI_STORE_F32, PAIR>(ta, tb, td, tr, g, st); break;
+    case EPI_ACC_F32: launch<BN, ST, A_MN, B_MN, EPI_ACC_F32, PAIR>(ta, tb, td, tr, g, st); break;
     case EPI_RESIDUAL:
-      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_RESIDUAL, PAIR>(ta, tb, td, g, st); break; }
+      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_RESIDUAL, PAIR>(ta, tb, td, tr, g, st); break; }
       TORCH_CHECK(false, "residual epilogue needs K-major operands");
     case EPI_ROPE:
-      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_ROPE, PAIR>(ta, tb, td, g, st); break; }
+      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_ROPE, PAIR>(ta, tb, td, tr, g, st); break; }
       TORCH_CHECK(false, "rope epilogue needs K-major operands");
     case EPI_SWIGLU:
-      if constexpr (!A_MN && !B_MN && BN == 256) { launch<BN, ST, A_MN, B_MN, EPI_SWIGLU, PAIR>(ta, tb, td, g, st); break; }
+      if constexpr (!A_MN && !B_MN && BN == 256) { launch<BN, ST, A_MN, B_MN, EPI_SWIGLU, PAIR>(ta, tb, td, tr, g, st); break; }
       TORCH_CHECK(false, "swiglu epilogue needs K-major operands and BN=256");
     case EPI_PEER_AR:
-      if constexpr (!A_MN) { launch<BN, ST, A_MN, B_MN, EPI_PEER_AR, PAIR>(ta, tb, td, g, st); break; }
+      if constexpr (!A_MN) { launch<BN, ST, A_MN, B_MN, EPI_PEER_AR, PAIR>(ta, tb, td, tr, g, st); break; }
       TORCH_CHECK(false, "peer all-reduce epilogue needs a K-major A operand");
     case EPI_CE_STATS:
-      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_CE_STATS, PAIR>(ta, tb, td, g, st); break; }
+      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_CE_STATS, PAIR>(ta, tb, td, tr, g, st); break; }
       TORCH_CHECK(false, "cross-entropy epilogues need K-major operands");
     case EPI_CE_GRAD:
-      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_CE_GRAD, PAIR>(ta, tb, td, g, st); break; }
+      if constexpr (!A_MN && !B_MN) { launch<BN, ST, A_MN, B_MN, EPI_CE_GRAD, PAIR>(ta, tb, td, tr, g, st); break; }
       TORCH_CHECK(false, "cross-entropy epilogues need K-major operands");
     case EPI_ACC_BF16OUT:
-      if constexpr (!A_MN && B_MN) { launch<BN, ST, A_MN, B_MN, EPI_ACC_BF16OUT, PAIR>(ta, tb, td, g, st); break; }
+      if constexpr (!A_MN && B_MN) { launch<BN, ST, A_MN, B_MN, EPI_ACC_BF16OUT, PAIR>(ta, tb, td, tr, g, st); break; }
       TORCH_CHECK(false, "fp32-accumulator epilogue is built for the input-gradient layout (A K-major, B MN-major)");
     default: DTB_CHECK(false, "unknown epilogue %d", epi);
   }
@@ -1275,14 +1421,14 @@ static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, 
 // all-gather -> GEMM launches (K-major operands; the epilogues the column-parallel
 // layers use)
 template <int BN, bool PAIR>
-static void dispatch_epi_ag(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
+static void dispatch_epi_ag(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const CUtensorMap& tr,
                             GemmArgs& g, cudaStream_t st) {
   constexpr int ST = (BN == 256 && !PAIR) ? 4 : kStages32K;
   switch (epi) {
-    case EPI_STORE_BF16: launch<BN, ST, false, false, EPI_STORE_BF16, PAIR, true>(ta, tb, td, g, st); break;
-    case EPI_ROPE: launch<BN, ST, false, false, EPI_ROPE, PAIR, true>(ta, tb, td, g, st); break;
+    case EPI_STORE_BF16: launch<BN, ST, false, false, EPI_STORE_BF16, PAIR, true>(ta, tb, td, tr, g, st); break;
+    case EPI_ROPE: launch<BN, ST, false, false, EPI_ROPE, PAIR, true>(ta, tb, td, tr, g, st); break;
     case EPI_SWIGLU:
-      if constexpr (BN == 256) { launch<BN, ST, false, false, EPI_SWIGLU, PAIR, true>(ta, tb, td, g, st); break; }
+      if constexpr (BN == 256) { launch<BN, ST, false, false, EPI_SWIGLU, PAIR, true>(ta, tb, td, tr, g, st); break; }
       TORCH_CHECK(false, "swiglu epilogue needs BN=256");
     default: DTB_CHECK(false, "all-gather GEMM: epilogue %d not built", epi);
   }
@@ -1348,7 +1494,24 @@ static bool pair_enabled() {
   return v == 1;
 }
 
+// TMA-store epilogues (store / accumulate / residual) unless DTB_GEMM_TMA_EPI=0;
+// gemm_tma_epilogue() switches them at run time (tests compare both paths)
+static int g_tma_epi = -1;
+static bool tma_epi_enabled() {
+  if (g_tma_epi < 0) {
+    const char* e = getenv("DTB_GEMM_TMA_EPI");
+    g_tma_epi = (e == nullptr || e[0] != '0') ? 1 : 0;
+  }
+  return g_tma_epi == 1;
+}
+
 }  // namespace dtb
+
+bool gemm_tma_epilogue(bool on) {
+  const bool prev = dtb::tma_epi_enabled();
+  dtb::g_tma_epi = on ? 1 : 0;
+  return prev;
+}
 
 // Python entry: see ops/gemm.py for the operand conventions.
 //   A: [M,K] (a_mn=false) or [K,M] (a_mn=true); B: [N,K] or [K,N]; D: [M,N]
@@ -1551,29 +1714,36 @@ static void gemm_impl(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_
             (int)a_mn, (int)b_mn, e, BN, A.data_ptr(), B.data_ptr(), D.data_ptr(), (const void*)g.alpha);
   const CUtensorMap ta = a_mn ? make_map(A.data_ptr(), M, K, A.stride(0), BK) : make_map(A.data_ptr(), K, M, A.stride(0), BM);
   const CUtensorMap tb = b_mn ? make_map(B.data_ptr(), NB, K, B.stride(0), BK) : make_map(B.data_ptr(), K, NB, B.stride(0), 128);
-  // bf16 store epilogue: D through [32 rows x 64 columns] TMA stores (other epilogues ignore td)
-  const CUtensorMap td = e == EPI_STORE_BF16 ? make_map(D.data_ptr(), g.N, D.size(0), D.stride(0), 32) : ta;
+  // store / accumulate / residual epilogues: D (and R) through TMA boxes when both
+  // can be described by a tensor map; split-K keeps the row-per-thread epilogue
+  CUtensorMap td = ta, tr = ta;
+  g.d_tma = 0;
+  if (tma_store_epi(e) && g.ksplit == 1 && tma_epi_enabled()) {
+    bool ok = make_out_map(&td, D.data_ptr(), f32out, g.N, D.size(0), D.stride(0));
+    if (ok && e == EPI_RESIDUAL) ok = make_out_map(&tr, R->data_ptr(), false, g.N, R->size(0), R->stride(0));
+    g.d_tma = ok ? 1 : 0;
+  }
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (ag != nullptr) {
-    if (BN == 256 && pair) dispatch_epi_ag<256, true>(e, ta, tb, td, g, st);
-    else if (BN == 256) dispatch_epi_ag<256, false>(e, ta, tb, td, g, st);
-    else dispatch_epi_ag<128, false>(e, ta, tb, td, g, st);
+    if (BN == 256 && pair) dispatch_epi_ag<256, true>(e, ta, tb, td, tr, g, st);
+    else if (BN == 256) dispatch_epi_ag<256, false>(e, ta, tb, td, tr, g, st);
+    else dispatch_epi_ag<128, false>(e, ta, tb, td, tr, g, st);
     return;
   }
   if (BN == 256 && pair) {
-    if (!a_mn && !b_mn) dispatch_epi<256, false, false, true>(e, ta, tb, td, g, st);
-    else if (!a_mn && b_mn) dispatch_epi<256, false, true, true>(e, ta, tb, td, g, st);
-    else if (a_mn && b_mn) dispatch_epi<256, true, true, true>(e, ta, tb, td, g, st);
+    if (!a_mn && !b_mn) dispatch_epi<256, false, false, true>(e, ta, tb, td, tr, g, st);
+    else if (!a_mn && b_mn) dispatch_epi<256, false, true, true>(e, ta, tb, td, tr, g, st);
+    else if (a_mn && b_mn) dispatch_epi<256, true, true, true>(e, ta, tb, td, tr, g, st);
     else TORCH_CHECK(false, "gemm: layout (MN, K) not built");
   } else if (BN == 256) {
-    if (!a_mn && !b_mn) dispatch_epi<256, false, false, false>(e, ta, tb, td, g, st);
-    else if (!a_mn && b_mn) dispatch_epi<256, false, true, false>(e, ta, tb, td, g, st);
-    else if (a_mn && b_mn) dispatch_epi<256, true, true, false>(e, ta, tb, td, g, st);
+    if (!a_mn && !b_mn) dispatch_epi<256, false, false, false>(e, ta, tb, td, tr, g, st);
+    else if (!a_mn && b_mn) dispatch_epi<256, false, true, false>(e, ta, tb, td, tr, g, st);
+    else if (a_mn && b_mn) dispatch_epi<256, true, true, false>(e, ta, tb, td, tr, g, st);
     else TORCH_CHECK(false, "gemm: layout (MN, K) not built");
   } else {
-    if (!a_mn && !b_mn) dispatch_epi<128, false, false, false>(e, ta, tb, td, g, st);
-    else if (!a_mn && b_mn) dispatch_epi<128, false, true, false>(e, ta, tb, td, g, st);
-    else if (a_mn && b_mn) dispatch_epi<128, true, true, false>(e, ta, tb, td, g, st);
+    if (!a_mn && !b_mn) dispatch_epi<128, false, false, false>(e, ta, tb, td, tr, g, st);
+    else if (!a_mn && b_mn) dispatch_epi<128, false, true, false>(e, ta, tb, td, tr, g, st);
+    else if (a_mn && b_mn) dispatch_epi<128, true, true, false>(e, ta, tb, td, tr, g, st);
     else TORCH_CHECK(false, "gemm: layout (MN, K) not built");
   }
 }

@@ -105,6 +105,49 @@ def _split_k_shape(M, N, K):
         assert torch.equal(again, acc)
 
 
+@pytest.mark.parametrize("M,N,K", [(200, 136, 96), (1000, 96, 512), (4096, 4096, 1024), (384, 4104, 256)])
+def test_gemm_tma_epilogues_match_row_path(M, N, K):
+    """Store (bf16, fp32), TMA reduce-add accumulate and residual epilogues through TMA
+    boxes give the same bits as the row-per-thread epilogues, and match the fp32 oracle;
+    partial boxes at the right and bottom edges are clipped by the tensor map."""
+    a, b, r = _rand(M, K), _rand(N, K), _rand(M, N)
+    at, bt = _rand(K, M), _rand(K, N)
+    alpha = torch.tensor([0.375], device=DEV)
+    base = torch.randn(M, N, device=DEV)
+
+    def run():
+        out = {}
+        out["bf16"] = gemm.mm_nt(a, b)
+        out["f32"] = gemm.mm_nt(a, b, out_dtype=torch.float32)
+        res = torch.empty(M, N, device=DEV, dtype=BF)
+        native().gemm(a, b, res, False, False, gemm.EPI_RESIDUAL, r, alpha, None, None, None, 0, 0)
+        out["res"] = res
+        acc = base.clone()
+        gemm.mm_tn_acc(at, bt, acc, alpha=alpha)
+        out["acc"] = acc
+        st = torch.empty(M, N, device=DEV)
+        gemm.mm_tn_acc(at, bt, st, store=True)
+        out["st"] = st
+        return out
+
+    prev = native().gemm_tma_epilogue(True)
+    try:
+        tma = run()
+        native().gemm_tma_epilogue(False)
+        row = run()
+    finally:
+        native().gemm_tma_epilogue(prev)
+    for k in tma:
+        assert torch.equal(tma[k], row[k]), k
+    ref = a.float() @ b.float().t()
+    reft = at.float().t() @ bt.float()
+    assert _rel(tma["bf16"], ref) < 1e-2
+    assert _rel(tma["f32"], ref) < 1e-5
+    assert _rel(tma["res"], 0.375 * ref + r.float()) < 1e-2
+    assert _rel(tma["acc"], base + 0.375 * reft) < 1e-5
+    assert _rel(tma["st"], reft) < 1e-5
+
+
 def test_tmem_a_operand_layout():
     """tcgen05 MMA reading A from tensor memory in the softmax threads' layout (row = lane,
     bf16 pairs per 32-bit column) equals the fp32 product."""
