@@ -311,6 +311,11 @@ class TPComm:
         # exceeds two-shot's 2(tp-1)/tp; DTB_TP_TWO_SHOT=0/1 overrides
         env = os.environ.get("DTB_TP_TWO_SHOT")
         self.two_shot = (env == "1") if env in ("0", "1") else self.size >= 4
+        # the layers use the fused all-reduces (GEMM + all-reduce, dgrad + all-reduce, standalone)
+        # up to tp = 4; at tp = 8 GEMM + NCCL all-reduce measured faster in every 7B shape
+        # (0.31-0.37 ms against 0.39-0.48 ms two-shot, tests/performance/bench_fused_comm.py),
+        # so they take that path there.  DTB_TP_FUSED_AR_MAX moves the limit.
+        self.fused_ar = self.size <= int(os.environ.get("DTB_TP_FUSED_AR_MAX", "4"))
         slot = _align(self.max_elems * 2)
         self.heap = SymmetricHeap(group, 2 * slot + self.flag_bytes + 64 * 1024, device)
         self.slots = [self.heap.alloc(slot), self.heap.alloc(slot)]

@@ -178,8 +178,13 @@ def _reduce_scatter_rows(x: torch.Tensor, tp: TPInfo) -> torch.Tensor:
     return full[tp.rank * rows:(tp.rank + 1) * rows].contiguous()
 
 
+def _fused_ar(tp: TPInfo) -> bool:
+    """The NVLink transport's fused all-reduces apply (see ``TPComm.fused_ar``)."""
+    return tp.comm is not None and getattr(tp.comm, "fused_ar", True)
+
+
 def _all_reduce(x: torch.Tensor, tp: TPInfo) -> torch.Tensor:
-    if tp.fused and x.is_cuda and tp.comm is not None:
+    if tp.fused and x.is_cuda and _fused_ar(tp):
         return tp.comm.all_reduce(x)
     x = x.contiguous()
     dist.all_reduce(x, group=tp.group)
@@ -284,7 +289,9 @@ def column_input_fused(x2: torch.Tensor, tp: TPInfo | None, sp_ok: bool = True) 
     the gather and the gradient's reduce-scatter are fused into the layer's GEMMs."""
     if tp is not None and tp.size > 1 and tp.fused and tp.comm is not None and x2.is_cuda:
         if not tp.sequence_parallel:
-            return x2, tp.comm
+            if _fused_ar(tp):
+                return x2, tp.comm
+            return column_input(x2, tp), None
         if sp_ok and hasattr(tp.comm, "sp_fusable") and tp.comm.sp_fusable(x2):
             return x2, SPColumn(tp.comm)
     return column_input(x2, tp), None
@@ -305,7 +312,7 @@ def row_output_linear(x2: torch.Tensor, weight: torch.Tensor, residual: torch.Te
     """``reduce(x2 @ W^T) (+ bias) (+ residual)`` for a row-parallel weight."""
     if tp is None or tp.size == 1:
         return linear(x2, weight, bias=bias, residual=residual, main_grad=main_grad)
-    if tp.fused and x2.is_cuda and tp.comm is not None and bias is None:
+    if tp.fused and x2.is_cuda and tp.comm is not None and bias is None and (tp.sequence_parallel or _fused_ar(tp)):
         return tp.comm.row_parallel_linear(x2, weight, residual, main_grad)
     y = linear(x2, weight, main_grad=main_grad)
     y = _SeqReduceScatter.apply(y, tp) if tp.sequence_parallel else _AllReduceFwd.apply(y, tp)

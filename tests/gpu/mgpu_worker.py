@@ -139,7 +139,8 @@ def main():
         for fused in (True, False):
             cfg = TrainingConfig.from_yaml(os.path.join(root, "config", "test_tiny.yaml"))
             cfg.model.vocab_size, cfg.model.d_model, cfg.model.n_layers = 1024, 512, 2
-            cfg.model.n_heads, cfg.model.n_kv_heads, cfg.model.ffn_hidden_size = 8, 4, 1024
+            # 4 KV heads up to tp = 4; at tp = 8 every rank needs one of its own
+            cfg.model.n_heads, cfg.model.n_kv_heads, cfg.model.ffn_hidden_size = 8, max(4, tp), 1024
             # 1024 tokens per step: 256-row slices per rank up to tp=4, so sequence parallelism
             # takes the fused all-gather GEMM and dgrad reduce-scatter paths
             cfg.model.max_seq_len = 512

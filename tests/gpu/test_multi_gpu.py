@@ -27,6 +27,13 @@ def test_bounded_wait_times_out_and_reports():
     assert float(torch.ones(3, device="cuda").sum()) == 3.0
 
 
+
+def _failure_text(r) -> str:
+    """The ranks' exception lines first (torchrun's summary hides them), then the output tails."""
+    errs = [ln for ln in r.stderr.splitlines() if "Error" in ln or "error:" in ln][:40]
+    return "\n".join(errs) + "\n---\n" + r.stdout[-2000:] + r.stderr[-2000:]
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_peer_collectives_and_fused_gemm_allreduce_match_nccl():
     n = min(torch.cuda.device_count(), 8)
@@ -34,4 +41,4 @@ def test_peer_collectives_and_fused_gemm_allreduce_match_nccl():
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
            "--master-addr", "127.0.0.1", "--master-port", "29671", os.path.join(HERE, "mgpu_worker.py")]
     r = subprocess.run(["timeout", "-k", "30", "600"] + cmd, env=env, capture_output=True, text=True)
-    assert r.returncode == 0 and "MGPU_OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+    assert r.returncode == 0 and "MGPU_OK" in r.stdout, _failure_text(r)

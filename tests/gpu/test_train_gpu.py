@@ -15,6 +15,12 @@ if not torch.cuda.is_available():  # pragma: no cover
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
+def _failure_text(r) -> str:
+    """The ranks' exception lines first (torchrun's summary hides them), then the output tails."""
+    errs = [ln for ln in r.stderr.splitlines() if "Error" in ln or "error:" in ln][:40]
+    return "\n".join(errs) + "\n---\n" + r.stdout[-2000:] + r.stderr[-2000:]
+
+
 @pytest.mark.parametrize("n,tp", [(1, 1), (2, 2), (4, 2)])
 def test_resume_and_checkpointing_are_bit_exact(n, tp):
     if torch.cuda.device_count() < n:
@@ -23,4 +29,4 @@ def test_resume_and_checkpointing_are_bit_exact(n, tp):
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
            "--master-addr", "127.0.0.1", "--master-port", str(29681 + n), os.path.join(HERE, "train_worker.py")]
     r = subprocess.run(["timeout", "-k", "30", "600"] + cmd, env=env, capture_output=True, text=True)
-    assert r.returncode == 0 and "TRAIN_OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+    assert r.returncode == 0 and "TRAIN_OK" in r.stdout, _failure_text(r)
