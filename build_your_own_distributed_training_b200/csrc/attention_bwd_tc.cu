@@ -127,8 +127,10 @@ __global__ void __launch_bounds__(320, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkb = a.S / BKV;
-  const int kb = nkb - 1 - blockIdx.x;  // tiles near the end have the least work: start the others first
-  const int hk = blockIdx.y, b = blockIdx.z;
+  // grid (kv heads x batch, key tiles): tiles near the end have the least work,
+  // and blocks start in linear order, so every head's longer tiles start first
+  const int kb = nkb - 1 - blockIdx.y;
+  const int hk = blockIdx.x % a.nkv, b = blockIdx.x / a.nkv;
   const int grp = a.nq / a.nkv;
   const int kv0 = kb * BKV;
   const int q_first = kv0 / BQ;
@@ -417,8 +419,10 @@ __global__ void __launch_bounds__(320, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkb = a.S / BKV;
-  const int kb = nkb - 1 - blockIdx.x;  // tiles near the end have the least work: start the others first
-  const int hk = blockIdx.y, b = blockIdx.z;
+  // grid (kv heads x batch, key tiles): tiles near the end have the least work,
+  // and blocks start in linear order, so every head's longer tiles start first
+  const int kb = nkb - 1 - blockIdx.y;
+  const int hk = blockIdx.x % a.nkv, b = blockIdx.x / a.nkv;
   const int grp = a.nq / a.nkv;
   const int kv0 = kb * BKV;
   const int nqt = a.S / BQ - kb;        // query tiles from the diagonal one
@@ -664,8 +668,8 @@ __global__ void __launch_bounds__(320, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool tr = a.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
   const int nqb = a.S / BQ;
-  const int qb = nqb - 1 - blockIdx.x;
-  const int h = blockIdx.y, b = blockIdx.z;
+  const int qb = nqb - 1 - blockIdx.y;  // grid (heads x batch, query tiles): longest rows first
+  const int h = blockIdx.x % a.nq, b = blockIdx.x / a.nq;
   const int hk = h / (a.nq / a.nkv);
   const int q0 = qb * BQ;
   const int nkt = (q0 + BQ) / BKV;
@@ -911,8 +915,8 @@ __global__ void __launch_bounds__(320, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool tr = a.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
   const int nqb = a.S / BQ;
-  const int qb = nqb - 1 - blockIdx.x;
-  const int h = blockIdx.y, b = blockIdx.z;
+  const int qb = nqb - 1 - blockIdx.y;  // grid (heads x batch, query tiles): longest rows first
+  const int h = blockIdx.x % a.nq, b = blockIdx.x / a.nq;
   const int hk = h / (a.nq / a.nkv);
   const int q0 = qb * BQ;
   const int nkt = qb + 1;                 // causal: key tiles 0..qb
@@ -1198,17 +1202,17 @@ void bwd_tc_launch(const torch::Tensor& qkv, const torch::Tensor& dO, const floa
                                     SmKVT<HD>::TOTAL));
       cfg_tm = true;
     }
-    attn_bwd_dkdv_tm_kernel<HD><<<dim3(S / 128, nkv, B), 320, SmKVT<HD>::TOTAL, st>>>(kv128, kv128, do128, args);
+    attn_bwd_dkdv_tm_kernel<HD><<<dim3(nkv * B, S / 128, 1), 320, SmKVT<HD>::TOTAL, st>>>(kv128, kv128, do128, args);
   } else {
-    attn_bwd_dkdv_tc_kernel<HD><<<dim3(S / 128, nkv, B), 320, SmKV<HD>::TOTAL, st>>>(kv128, q64, do64, args);
+    attn_bwd_dkdv_tc_kernel<HD><<<dim3(nkv * B, S / 128, 1), 320, SmKV<HD>::TOTAL, st>>>(kv128, q64, do64, args);
   }
   DTB_LAUNCH_CHECK();
   if (dq128)
-    attn_bwd_dq128_tc_kernel<HD><<<dim3(S / 128, nq, B), 320, SmQ128<HD>::TOTAL, st>>>(kv128, do128, kv128, args);
+    attn_bwd_dq128_tc_kernel<HD><<<dim3(nq * B, S / 128, 1), 320, SmQ128<HD>::TOTAL, st>>>(kv128, do128, kv128, args);
   else if (dq_stages == 3)
-    attn_bwd_dq_tc_kernel<HD, 3><<<dim3(S / 128, nq, B), 320, SmQ<HD, 3>::TOTAL, st>>>(kv128, do128, q64, args);
+    attn_bwd_dq_tc_kernel<HD, 3><<<dim3(nq * B, S / 128, 1), 320, SmQ<HD, 3>::TOTAL, st>>>(kv128, do128, q64, args);
   else
-    attn_bwd_dq_tc_kernel<HD, 4><<<dim3(S / 128, nq, B), 320, SmQ<HD, 4>::TOTAL, st>>>(kv128, do128, q64, args);
+    attn_bwd_dq_tc_kernel<HD, 4><<<dim3(nq * B, S / 128, 1), 320, SmQ<HD, 4>::TOTAL, st>>>(kv128, do128, q64, args);
   DTB_LAUNCH_CHECK();
   if (trace_on) {
     // diagnostic: per-iteration phase times (SM cycles) of the dQ kernel's first CTA

@@ -120,8 +120,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nqb = a.S / BM;
-  const int qb = nqb - 1 - blockIdx.x;  // longest rows first
-  const int h = blockIdx.y, b = blockIdx.z;
+  // grid (heads x batch, query tiles): blocks start in linear order, so every
+  // head's longest rows start before any head's shorter ones (longest first
+  // over the whole grid, which shortens the last wave of this causal workload)
+  const int qb = nqb - 1 - blockIdx.y;
+  const int h = blockIdx.x % a.nq, b = blockIdx.x / a.nq;
   const int hk = h / (a.nq / a.nkv);
   const int nkb = qb + 1;               // kv tiles 0..qb (causal, BN == BM)
   const int row0 = b * a.S;             // first packed row of this sequence
@@ -461,8 +464,8 @@ __global__ void __launch_bounds__(320, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int npairs = a.S / (2 * BM);
-  const int pr = npairs - 1 - blockIdx.x;  // longest rows first
-  const int h = blockIdx.y, b = blockIdx.z;
+  const int pr = npairs - 1 - blockIdx.y;  // longest rows first over the whole grid
+  const int h = blockIdx.x % a.nq, b = blockIdx.x / a.nq;
   const int hk = h / (a.nq / a.nkv);
   const int qb0 = 2 * pr;                  // tile A; tile B = qb0 + 1
   const int nkb_a = qb0 + 1, nkb_b = qb0 + 2;
@@ -783,7 +786,7 @@ void fwd_tc_launch(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& ls
     }
     FwdArgs args{reinterpret_cast<__nv_bfloat16*>(o.data_ptr()), lse.data_ptr<float>(), S, nq, nkv, scale * LOG2E,
                  dtb_error_word()};
-    attn_fwd_pp_kernel<HD><<<dim3(S / (2 * BM), nq, B), 320, LP::TOTAL, at::cuda::getCurrentCUDAStream()>>>(tqk, tv,
+    attn_fwd_pp_kernel<HD><<<dim3(nq * B, S / (2 * BM), 1), 320, LP::TOTAL, at::cuda::getCurrentCUDAStream()>>>(tqk, tv,
                                                                                                             args);
     DTB_LAUNCH_CHECK();
     return;
@@ -795,7 +798,7 @@ void fwd_tc_launch(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& ls
   }
   FwdArgs args{reinterpret_cast<__nv_bfloat16*>(o.data_ptr()), lse.data_ptr<float>(), S, nq, nkv, scale * LOG2E,
                dtb_error_word()};
-  attn_fwd_tc_kernel<HD><<<dim3(S / BM, nq, B), NTHREADS, L::TOTAL, at::cuda::getCurrentCUDAStream()>>>(tqk, tv,
+  attn_fwd_tc_kernel<HD><<<dim3(nq * B, S / BM, 1), NTHREADS, L::TOTAL, at::cuda::getCurrentCUDAStream()>>>(tqk, tv,
                                                                                                         args);
   DTB_LAUNCH_CHECK();
 }

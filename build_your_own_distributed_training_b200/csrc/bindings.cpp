@@ -1,7 +1,7 @@
 // Python bindings of the native extension.
 #include <torch/extension.h>
 
-bool gemm_tma_epilogue(bool on);
+int64_t gemm_tma_epilogue(int64_t level);
 void gemm_entry(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_mn, bool b_mn, int64_t epi,
                 c10::optional<torch::Tensor> R, c10::optional<torch::Tensor> alpha,
                 c10::optional<torch::Tensor> cos_t, c10::optional<torch::Tensor> sin_t,
@@ -66,7 +66,7 @@ void ce_loss_finish(torch::Tensor row_loss, torch::Tensor labels, int64_t vocab_
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels for B200-native 2-D parallel LLaMA training";
   m.def("gemm", &gemm_entry, "tcgen05 GEMM with fused epilogues");
-  m.def("gemm_tma_epilogue", &gemm_tma_epilogue, "switch the TMA-store GEMM epilogues; returns the previous setting");
+  m.def("gemm_tma_epilogue", &gemm_tma_epilogue, "TMA-store GEMM epilogue level (0 none, 1 store/accumulate/residual, 2 also RoPE/SwiGLU); returns the previous level");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("rope_bwd", &rope_bwd);

@@ -96,7 +96,7 @@ struct GemmArgs {
   int* sk_flags;
   uint32_t sk_epoch;
   int d_v8;               // fp32 D: base 32-byte aligned and ldd % 8 == 0 (256-bit stores)
-  int d_tma;              // store / accumulate / residual epilogues: D (and R) go through tensor maps
+  int d_tma;              // tma_store_epi epilogues: D (and R or D2) go through tensor maps
   // AG (all-gather fused in front of the GEMM, sequence parallelism): A is the
   // gathered [M, K] buffer `ag_out`, filled by the kernel's copier warps from this
   // rank's rows `ag_local` and the peers' staged rows (peer_base[p] + stage_off)
@@ -129,7 +129,8 @@ __device__ __forceinline__ void tile_coords(int tile, int mblocks, int nblocks, 
 
 // epilogues whose output leaves through TMA bulk stores (when args.d_tma is set)
 __host__ __device__ constexpr bool tma_store_epi(int epi) {
-  return epi == EPI_STORE_BF16 || epi == EPI_STORE_F32 || epi == EPI_ACC_F32 || epi == EPI_RESIDUAL;
+  return epi == EPI_STORE_BF16 || epi == EPI_STORE_F32 || epi == EPI_ACC_F32 || epi == EPI_RESIDUAL ||
+         epi == EPI_ROPE || epi == EPI_SWIGLU;
 }
 
 // TSTORE: 4 KB of shared memory per epilogue warp for the TMA-store epilogues
@@ -224,6 +225,16 @@ __device__ __forceinline__ void store_bf16_32(__nv_bfloat16* p, const float (&v)
   }
 }
 
+// rotate-half RoPE of the pair (x1, x2) = (column p, column p + hd/2) of a head,
+// each product rounded on its own (no contraction) so every epilogue gives the same bits
+__device__ __forceinline__ float rope_lo(float x1, float x2, float c, float s) {
+  return __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+}
+__device__ __forceinline__ float rope_hi(float x1, float x2, float c, float s) {
+  return __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+}
+__device__ __forceinline__ float swiglu_h(float gr, float ur) { return __fdividef(gr, 1.f + __expf(-gr)) * ur; }
+
 template <int BN, int EPI>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase, int mb, int nb, int quad,
                                               int lane) {
@@ -253,7 +264,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
         for (int i = 0; i < 32; ++i) {
           gr[i] = __bfloat162float(__float2bfloat16_rn(g[i]));
           ur[i] = __bfloat162float(__float2bfloat16_rn(u[i]));
-          h[i] = __fdividef(gr[i], 1.f + __expf(-gr[i])) * ur[i];
+          h[i] = swiglu_h(gr[i], ur[i]);
         }
         store_bf16_32(gp, gr);
         store_bf16_32(up, ur);
@@ -386,8 +397,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t tbase,
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               const float x1 = __uint_as_float(r1[i]), x2 = __uint_as_float(r2[i]);
-              y1[i] = x1 * cs[i] - x2 * sn[i];
-              y2[i] = x2 * cs[i] + x1 * sn[i];
+              y1[i] = rope_lo(x1, x2, cs[i], sn[i]);
+              y2[i] = rope_hi(x1, x2, cs[i], sn[i]);
             }
             __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(a.D) + (long)row * a.ldd + col + j;
             store_bf16_32(p, y1);
@@ -629,6 +640,143 @@ __device__ __forceinline__ void epilogue_tma_residual(const GemmArgs& a, const C
       tma_store_2d(tmD, stg, n0 + c, grow0);
       bulk_commit_group();
     }
+  }
+}
+
+// Writes 64 bf16 (packed pairs) as this lane's row of a 128-byte-swizzled
+// [32 x 64] box in the warp's staging slot, then one lane stores the box at
+// (x, y) through `m`.  The slot's previous store must have read it: checked here.
+__device__ __forceinline__ void stage_and_store_row64(const CUtensorMap* m, uint8_t* stg, const uint32_t (&pk)[32],
+                                                      int x, int y, int lane) {
+  if (lane == 0) bulk_wait_group_read0();
+  __syncwarp();
+  uint8_t* rowp = stg + lane * 128;
+#pragma unroll
+  for (int cc = 0; cc < 8; ++cc)
+    *reinterpret_cast<uint4*>(rowp + ((cc ^ (lane & 7)) << 4)) =
+        make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(m, stg, x, y);
+    bulk_commit_group();
+  }
+}
+
+// QKV projection with RoPE on the first rope_cols columns: each 64-column box of
+// the output is produced in two 32-column halves; a rotated half needs both
+// members of its pairs (columns p and p + hd/2 of the head), so the TMEM
+// columns are read once per output half instead of once per pair.
+template <int BN>
+__device__ __forceinline__ void epilogue_tma_rope(const GemmArgs& a, const CUtensorMap* tmD, uint8_t* stg,
+                                                  uint32_t tbase, int mb, int nb, int quad, int lane) {
+  const uint32_t trow = tbase + ((uint32_t)(quad * 32) << 16);
+  const int n0 = nb * BN;
+  const int grow0 = mb * BM + quad * 32;
+  const int hd = a.head_dim, half = hd >> 1;
+  const int pos = (grow0 + lane) % a.seqlen;  // rows past M read valid table rows and are clipped on store
+  const float4* crow = reinterpret_cast<const float4*>(a.cos_t + (long)pos * hd);
+  const float4* srow = reinterpret_cast<const float4*>(a.sin_t + (long)pos * hd);
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 64) {
+    const int col = n0 + c;
+    if (col >= a.N) break;
+    uint32_t pk[32];
+    if (col < a.rope_cols) {
+      const int h0 = (c / hd) * hd;  // head start inside the tile (hd % 64 == 0)
+#pragma unroll
+      for (int j = 0; j < 64; j += 32) {
+        const int e = c - h0 + j;  // element of the head
+        const bool lo = e < half;
+        const int p = lo ? e : e - half;
+        float4 c4[8], s4[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          c4[q] = __ldg(crow + (p >> 2) + q);
+          s4[q] = __ldg(srow + (p >> 2) + q);
+        }
+        uint32_t r1[32], r2[32];
+        tmem_ld32_async(trow + h0 + p, r1);
+        tmem_ld32_async(trow + h0 + half + p, r2);
+        tmem_wait_ld();
+        tmem_regs(r1);
+        tmem_regs(r2);
+        const float* cs = reinterpret_cast<const float*>(c4);
+        const float* sn = reinterpret_cast<const float*>(s4);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float x1a = __uint_as_float(r1[2 * i]), x2a = __uint_as_float(r2[2 * i]);
+          const float x1b = __uint_as_float(r1[2 * i + 1]), x2b = __uint_as_float(r2[2 * i + 1]);
+          const float ya = lo ? rope_lo(x1a, x2a, cs[2 * i], sn[2 * i]) : rope_hi(x1a, x2a, cs[2 * i], sn[2 * i]);
+          const float yb = lo ? rope_lo(x1b, x2b, cs[2 * i + 1], sn[2 * i + 1])
+                              : rope_hi(x1b, x2b, cs[2 * i + 1], sn[2 * i + 1]);
+          pk[(j >> 1) + i] = pack_bf16x2(ya, yb);
+        }
+      }
+    } else {
+      uint32_t r1[32], r2[32];
+      tmem_ld32_async(trow + c, r1);
+      tmem_ld32_async(trow + c + 32, r2);
+      tmem_wait_ld();
+      tmem_regs(r1);
+      tmem_regs(r2);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        pk[i] = pack_bf16x2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
+        pk[16 + i] = pack_bf16x2(__uint_as_float(r2[2 * i]), __uint_as_float(r2[2 * i + 1]));
+      }
+    }
+    stage_and_store_row64(tmD, stg, pk, col, grow0, lane);
+  }
+}
+
+// Gate/up projection with SwiGLU: TMEM columns [0,128) hold g and [128,256) u
+// for output columns nb*128 + [0,128).  Per 64 output columns three boxes leave
+// through the one staging slot: round(g) and round(u) into D2 = [g | u] (at
+// column c and ffn + c), then silu(g) * u into D, from the rounded values.
+template <int BN>
+__device__ __forceinline__ void epilogue_tma_swiglu(const GemmArgs& a, const CUtensorMap* tmD,
+                                                    const CUtensorMap* tmD2, uint8_t* stg, uint32_t tbase, int mb,
+                                                    int nb, int quad, int lane) {
+  const uint32_t trow = tbase + ((uint32_t)(quad * 32) << 16);
+  const int c0 = nb * 128;
+  const int grow0 = mb * BM + quad * 32;
+#pragma unroll 1
+  for (int c = 0; c < 128; c += 64) {
+    uint32_t pk[32];
+#pragma unroll 1
+    for (int which = 0; which < 2; ++which) {  // 0: g, 1: u
+      uint32_t r1[32], r2[32];
+      tmem_ld32_async(trow + which * 128 + c, r1);
+      tmem_ld32_async(trow + which * 128 + c + 32, r2);
+      tmem_wait_ld();
+      tmem_regs(r1);
+      tmem_regs(r2);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        pk[i] = pack_bf16x2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
+        pk[16 + i] = pack_bf16x2(__uint_as_float(r2[2 * i]), __uint_as_float(r2[2 * i + 1]));
+      }
+      stage_and_store_row64(tmD2, stg, pk, which * a.ffn + c0 + c, grow0, lane);
+    }
+#pragma unroll
+    for (int j = 0; j < 64; j += 32) {
+      uint32_t rg[32], ru[32];
+      tmem_ld32_async(trow + c + j, rg);
+      tmem_ld32_async(trow + 128 + c + j, ru);
+      tmem_wait_ld();
+      tmem_regs(rg);
+      tmem_regs(ru);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float ga = __bfloat162float(__float2bfloat16_rn(__uint_as_float(rg[2 * i])));
+        const float gb = __bfloat162float(__float2bfloat16_rn(__uint_as_float(rg[2 * i + 1])));
+        const float ua = __bfloat162float(__float2bfloat16_rn(__uint_as_float(ru[2 * i])));
+        const float ub = __bfloat162float(__float2bfloat16_rn(__uint_as_float(ru[2 * i + 1])));
+        pk[(j >> 1) + i] = pack_bf16x2(swiglu_h(ga, ua), swiglu_h(gb, ub));
+      }
+    }
+    stage_and_store_row64(tmD, stg, pk, c0 + c, grow0, lane);
   }
 }
 
@@ -1212,6 +1360,10 @@ __global__ void __launch_bounds__(AG ? 384 : 320, 1)
                                     rphase, tb, slab, nb, quad, lane, abort_flag);
         } else if constexpr (EPI == EPI_STORE_F32 || EPI == EPI_ACC_F32) {
           epilogue_tma_f32<BN, EPI == EPI_ACC_F32>(args, &tmD, stg, tb, slab, nb, quad, lane);
+        } else if constexpr (EPI == EPI_ROPE) {
+          epilogue_tma_rope<BN>(args, &tmD, stg, tb, slab, nb, quad, lane);
+        } else if constexpr (EPI == EPI_SWIGLU) {
+          if constexpr (BN == 256) epilogue_tma_swiglu<BN>(args, &tmD, &tmR, stg, tb, slab, nb, quad, lane);
         }
       } else if constexpr (EPI == EPI_STORE_F32 || EPI == EPI_ACC_F32) {
         if (split == 0) {
@@ -1494,22 +1646,25 @@ static bool pair_enabled() {
   return v == 1;
 }
 
-// TMA-store epilogues (store / accumulate / residual) unless DTB_GEMM_TMA_EPI=0;
-// gemm_tma_epilogue() switches them at run time (tests compare both paths)
+// TMA-store epilogues: level 1 (default) for store / accumulate / residual, level 2
+// also for RoPE and SwiGLU, 0 for none (DTB_GEMM_TMA_EPI=0/1/2).  The level-2 set is
+// built and checked against the row-per-thread path by its test, which runs it in
+// a child process; it becomes the default once that has passed on a B200.
+// gemm_tma_epilogue() sets the level at run time (tests compare the paths).
 static int g_tma_epi = -1;
-static bool tma_epi_enabled() {
+static int tma_epi_level() {
   if (g_tma_epi < 0) {
     const char* e = getenv("DTB_GEMM_TMA_EPI");
-    g_tma_epi = (e == nullptr || e[0] != '0') ? 1 : 0;
+    g_tma_epi = (e == nullptr) ? 1 : (e[0] == '0' ? 0 : (e[0] == '2' ? 2 : 1));
   }
-  return g_tma_epi == 1;
+  return g_tma_epi;
 }
 
 }  // namespace dtb
 
-bool gemm_tma_epilogue(bool on) {
-  const bool prev = dtb::tma_epi_enabled();
-  dtb::g_tma_epi = on ? 1 : 0;
+int64_t gemm_tma_epilogue(int64_t level) {
+  const int prev = dtb::tma_epi_level();
+  dtb::g_tma_epi = (int)std::max<int64_t>(0, std::min<int64_t>(2, level));
   return prev;
 }
 
@@ -1714,13 +1869,15 @@ static void gemm_impl(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_
             (int)a_mn, (int)b_mn, e, BN, A.data_ptr(), B.data_ptr(), D.data_ptr(), (const void*)g.alpha);
   const CUtensorMap ta = a_mn ? make_map(A.data_ptr(), M, K, A.stride(0), BK) : make_map(A.data_ptr(), K, M, A.stride(0), BM);
   const CUtensorMap tb = b_mn ? make_map(B.data_ptr(), NB, K, B.stride(0), BK) : make_map(B.data_ptr(), K, NB, B.stride(0), 128);
-  // store / accumulate / residual epilogues: D (and R) through TMA boxes when both
-  // can be described by a tensor map; split-K keeps the row-per-thread epilogue
+  // store / accumulate / residual / RoPE / SwiGLU epilogues: D (and R or D2) through TMA
+  // boxes when each can be described by a tensor map; split-K keeps the row-per-thread epilogue
   CUtensorMap td = ta, tr = ta;
   g.d_tma = 0;
-  if (tma_store_epi(e) && g.ksplit == 1 && tma_epi_enabled()) {
+  if (tma_store_epi(e) && g.ksplit == 1 && tma_epi_level() >= ((e == EPI_ROPE || e == EPI_SWIGLU) ? 2 : 1)) {
     bool ok = make_out_map(&td, D.data_ptr(), f32out, g.N, D.size(0), D.stride(0));
     if (ok && e == EPI_RESIDUAL) ok = make_out_map(&tr, R->data_ptr(), false, g.N, R->size(0), R->stride(0));
+    // SwiGLU: tr describes D2 = [g | u]
+    if (ok && e == EPI_SWIGLU) ok = make_out_map(&tr, D2->data_ptr(), false, 2L * g.ffn, D2->size(0), D2->stride(0));
     g.d_tma = ok ? 1 : 0;
   }
   cudaStream_t st = at::cuda::getCurrentCUDAStream();

@@ -130,10 +130,10 @@ def test_gemm_tma_epilogues_match_row_path(M, N, K):
         out["st"] = st
         return out
 
-    prev = native().gemm_tma_epilogue(True)
+    prev = native().gemm_tma_epilogue(1)
     try:
         tma = run()
-        native().gemm_tma_epilogue(False)
+        native().gemm_tma_epilogue(0)
         row = run()
     finally:
         native().gemm_tma_epilogue(prev)
@@ -146,6 +146,47 @@ def test_gemm_tma_epilogues_match_row_path(M, N, K):
     assert _rel(tma["res"], 0.375 * ref + r.float()) < 1e-2
     assert _rel(tma["acc"], base + 0.375 * reft) < 1e-5
     assert _rel(tma["st"], reft) < 1e-5
+
+
+@pytest.mark.parametrize("M,hd,seq", [(512, 128, 256), (300, 64, 300)])
+def test_gemm_tma_rope_swiglu_match_row_path(M, hd, seq):
+    """The RoPE and SwiGLU epilogues through TMA boxes (epilogue level 2, not yet the
+    default) give the row-per-thread bits.  Runs in a child process, so that a failure
+    of the new path cannot take this process's CUDA context with it."""
+    import subprocess
+    import sys
+    code = ("import sys; sys.path.insert(0, %r)\n" % os.path.dirname(os.path.dirname(os.path.dirname(
+        os.path.abspath(__file__)))) + "from tests.gpu.test_kernels import _tma_rope_swiglu_case\n"
+        "_tma_rope_swiglu_case(%d, %d, %d)\n" % (M, hd, seq))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "TMA_ROPE_SWIGLU_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+def _tma_rope_swiglu_case(M, hd, seq):
+    from build_your_own_distributed_training_b200.ops.rope import precompute_rope_cache
+    K, heads, ffn = 256, 4, 384
+    a = _rand(M, K)
+    wqkv = _rand(3 * heads * hd, K, scale=0.1)
+    wgu = _rand(2 * ffn, K, scale=0.1)
+    cos, sin = precompute_rope_cache(hd, seq, 10000.0, device=DEV)
+
+    def run():
+        q = gemm.mm_nt_rope(a, wqkv, cos, sin, 2 * heads * hd, hd, seq)
+        act, gu = gemm.mm_nt_swiglu(a, wgu, ffn)
+        return q, act, gu
+
+    native().gemm_tma_epilogue(2)
+    tma = run()
+    native().gemm_tma_epilogue(0)
+    row = run()
+    for name, x, y in zip(("rope", "act", "gu"), tma, row):
+        assert torch.equal(x, y), name
+    g, u = (a.float() @ wgu.float().t()).split(ffn, dim=1)
+    assert _rel(tma[2], torch.cat([g, u], 1)) < 1e-2
+    gr, ur = tma[2].float().split(ffn, dim=1)
+    assert _rel(tma[1], torch.nn.functional.silu(gr) * ur) < 1e-2
+    assert native().device_error() == 0
+    print("TMA_ROPE_SWIGLU_OK")
 
 
 def test_tmem_a_operand_layout():
