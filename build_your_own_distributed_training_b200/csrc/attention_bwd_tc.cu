@@ -80,6 +80,7 @@ struct BwdArgs {
   float scale, scale_log2;
   int* err;
   long long* trace;   // phase timestamps of one CTA (DTB_ATTN_TRACE=1), else nullptr
+  int early_s;        // dK/dV TMEM kernel: issue S^T of the next tile before dK of this one
 };
 
 // clock64 timestamp of phase k of iteration j for trace row `role`
@@ -486,20 +487,33 @@ __global__ void __launch_bounds__(320, 1)
       constexpr uint32_t ID_G = idesc_bf16(BKV, HD, false, true);    // dV, dK: A (TMEM) x B (dO / Q, MN-major)
       const uint32_t k0 = smem_u32(sm + L::K_OFF), v0 = smem_u32(sm + L::V_OFF);
       bool ok = mbar_wait(kv_full, 0, a.err);
-      for (int it = 0; it < total && ok && !*abort_flag; ++it) {
-        const int st = it % NS;
-        if (!mbar_wait(&q_full[st], (it / NS) & 1, a.err)) {
-          ok = false;
-          break;
-        }
+      // S^T of query tile `t` once its Q / dO stage has landed
+      auto issue_s = [&](int t) -> bool {
+        const int ss = t % NS;
+        if (!mbar_wait(&q_full[ss], (t / NS) & 1, a.err)) return false;
         tc_fence_after();
-        const uint32_t q0 = smem_u32(sm + L::Q_OFF + st * L::QT), o0 = smem_u32(sm + L::O_OFF + st * L::QT);
+        const uint32_t qs = smem_u32(sm + L::Q_OFF + ss * L::QT);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_bf16(t_s, sdesc_sw128(k0 + off, 16, 1024), sdesc_sw128(q0 + off, 16, 1024), ID_S, kk != 0);
+          umma_bf16(t_s, sdesc_sw128(k0 + off, 16, 1024), sdesc_sw128(qs + off, 16, 1024), ID_S, kk != 0);
         }
         umma_commit(s_full);
+        return true;
+      };
+      // early_s: per tile  dP^T(i) | P^T(i) written | dV(i)  S^T(i+1) | dS^T(i) written | dK(i),
+      // so the exponentials of tile i+1 run while the tensor pipe does dV(i), dK(i) and dP^T(i+1)
+      // (S^T(i+1) overwrites P^T(i) only after dV(i) has read it: the pipe runs in issue order;
+      // dP^T(i+1) overwrites dS^T(i) only after dK(i)).  Otherwise S^T(i+1) waits for dK(i).
+      const bool early = a.early_s != 0;
+      if (early && total > 0 && ok) ok = issue_s(0);
+      for (int it = 0; it < total && ok && !*abort_flag; ++it) {
+        const int st = it % NS;
+        if (!early && !issue_s(it)) {
+          ok = false;
+          break;
+        }
+        const uint32_t q0 = smem_u32(sm + L::Q_OFF + st * L::QT), o0 = smem_u32(sm + L::O_OFF + st * L::QT);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
@@ -517,6 +531,10 @@ __global__ void __launch_bounds__(320, 1)
         for (int kk = 0; kk < BQ / 16; ++kk) {
           const uint32_t ta = t_s + 64 * (kk >> 2) + 8 * (kk & 3);
           umma_bf16_ta(t_dv, ta, sdesc_sw128(o0 + kk * 2048, 16384, 1024), ID_G, (it | kk) != 0);
+        }
+        if (early && it + 1 < total && !issue_s(it + 1)) {
+          ok = false;
+          break;
         }
         if (!mbar_wait(ds_full, it & 1, a.err)) {
           ok = false;
@@ -1187,8 +1205,14 @@ void bwd_tc_launch(const torch::Tensor& qkv, const torch::Tensor& dO, const floa
   }();
   torch::Tensor trace;
   if (trace_on) trace = torch::zeros({4 * 64 * 8}, qkv.options().dtype(at::kLong));
+  // dK/dV TMEM kernel issue order (see attn_bwd_dkdv_tm_kernel): DTB_ATTN_DKDV_EARLY_S=1
+  static const int early_s = [] {
+    const char* e = getenv("DTB_ATTN_DKDV_EARLY_S");
+    return (e != nullptr && e[0] == '1') ? 1 : 0;
+  }();
   BwdArgs args{lse, Dv, reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), S, nq, nkv, scale, scale * LOG2E,
-               dtb_error_word(), trace_on ? reinterpret_cast<long long*>(trace.data_ptr<int64_t>()) : nullptr};
+               dtb_error_word(), trace_on ? reinterpret_cast<long long*>(trace.data_ptr<int64_t>()) : nullptr,
+               early_s};
   auto st = at::cuda::getCurrentCUDAStream();
   // dK/dV: 128-query tiles with P^T / dS^T in TMEM unless DTB_ATTN_DKDV_TM=0
   static const bool dkdv_tm = [] {

@@ -625,3 +625,35 @@ def test_attention_tcgen05_backward(b, s, nq, nkv, hd):
     assert _rel(d_tc, ref_in.grad) < 3e-2
     assert _rel(d_tc, d_legacy) < 2e-2
     assert torch.equal(d_tc, native().attn_bwd(do, qkv, o, lse, b, s, nq, nkv, hd, scale))
+
+
+def test_attention_backward_early_s_order_same_bits(tmp_path):
+    """The dK/dV kernel with the next tile's S^T issued before this tile's dK
+    (DTB_ATTN_DKDV_EARLY_S=1, read once per process: run in a child process) gives the
+    default order's bits."""
+    import subprocess
+    import sys
+    out = tmp_path / "early.pt"
+    code = ("import sys; sys.path.insert(0, %r)\n" % os.path.dirname(os.path.dirname(os.path.dirname(
+        os.path.abspath(__file__)))) + "from tests.gpu.test_kernels import _attn_bwd_case\n"
+        "import torch; torch.save(_attn_bwd_case(), %r)\n" % str(out))
+    r = subprocess.run([sys.executable, "-c", code], env=dict(os.environ, DTB_ATTN_DKDV_EARLY_S="1"),
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    early = torch.load(out)
+    for a_, b_ in zip(early, _attn_bwd_case()):
+        assert torch.equal(a_.to(DEV), b_)
+
+
+def _attn_bwd_case():
+    """Backward of three causal shapes (GQA, several key tiles) from fixed seeds."""
+    outs = []
+    for (b, s, nq, nkv, hd) in [(1, 1024, 4, 4, 128), (2, 512, 8, 2, 128), (1, 768, 4, 2, 64)]:
+        torch.manual_seed(11)
+        qkv = _rand(b * s, (nq + 2 * nkv) * hd)
+        do = _rand(b * s, nq * hd)
+        scale = 1 / math.sqrt(hd)
+        o, lse = native().attn_fwd(qkv, b, s, nq, nkv, hd, scale)
+        outs.append(native().attn_bwd(do, qkv, o, lse, b, s, nq, nkv, hd, scale))
+    assert native().device_error() == 0
+    return outs
