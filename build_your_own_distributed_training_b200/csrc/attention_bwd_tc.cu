@@ -360,16 +360,6 @@ __global__ void __launch_bounds__(320, 1)
 //   The exponentials of tile i overlap its dP^T product, the dS^T products its
 //   dV product.  Q / dO / lse / D: 2-deep ring.  Warp 0 loads, warp 1 owns
 //   TMEM and issues MMAs, warps 2-9 the elementwise part.  Bounded waits.
-__device__ __forceinline__ void umma_bf16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
-                                             uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
 __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&v)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "

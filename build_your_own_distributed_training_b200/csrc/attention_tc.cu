@@ -727,6 +727,324 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// ============================================================== two query tiles, P in TMEM
+// attn_fwd_ws_kernel: one CTA per (pair of adjacent 128-row query tiles, head,
+// batch), like attn_fwd_pp_kernel, with P kept in tensor memory:
+//   warp 0     TMA: Q_A, Q_B once; K_j and V_j into separate 2-deep rings
+//   warp 1     TMEM S_A [0,128) | S_B [128,256) | O_A [256, 256+hd) | O_B [256+hd, 256+2hd)
+//              and the MMAs, in the order S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j)
+//              S_B(j+1) | ...; PV reads P from TMEM as its A operand, so there is
+//              no shared-memory P buffer and V gets a second stage
+//   warps 2-5  softmax of tile A, warps 6-9 of tile B (thread = query row): two
+//              passes over the row's 128 scores, 32 columns at a time (row maximum,
+//              then exp2, row sum and P), so no thread holds the whole row; P goes
+//              back as bf16 pairs (score k in column k/2) into the first 64 columns
+//              of the tile's own S region, over scores the thread has already read
+// Ordering: S_X(j+1) overwrites P_X(j) only after PV_X(j) has read it (the tensor
+// pipe runs in issue order), and s_full_X(j) completes only after PV_X(j-1) (a
+// commit tracks every earlier MMA of the thread), so the softmax may rescale O_X
+// as soon as S_X(j) is there.  Same online softmax as attn_fwd_tc_kernel.
+template <int HD>
+struct SmemWS {
+  static constexpr int Q_BYTES = BM * HD * 2;
+  static constexpr int K_BYTES = BN * HD * 2;
+  static constexpr int V_BYTES = BN * HD * 2;
+  static constexpr int Q_OFF = 0;                         // Q_A, Q_B
+  static constexpr int K_OFF = Q_OFF + 2 * Q_BYTES;       // 2 stages
+  static constexpr int V_OFF = K_OFF + 2 * K_BYTES;       // 2 stages
+  static constexpr int BAR_OFF = V_OFF + 2 * V_BYTES;
+  static constexpr int N_BARS = 16;
+  static constexpr int TOTAL = BAR_OFF + N_BARS * 8 + 16 + 1024;
+  static_assert(TOTAL <= 232448, "shared memory per CTA");
+};
+
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+template <int HD>
+__global__ void __launch_bounds__(320, 1)
+    attn_fwd_ws_kernel(const __grid_constant__ CUtensorMap tm_qk, const __grid_constant__ CUtensorMap tm_v,
+                       const FwdArgs a) {
+  using L = SmemWS<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;     // [2 stages]
+  uint64_t* k_empty = bars + 3;    // [2 stages]
+  uint64_t* v_full = bars + 5;     // [2 stages]
+  uint64_t* v_empty = bars + 7;    // [2 stages]
+  uint64_t* s_full = bars + 9;     // [2 tiles]
+  uint64_t* p_full = bars + 11;    // [2 tiles]
+  uint64_t* pv_done = bars + 13;   // [2 tiles]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + L::N_BARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int npairs = a.S / (2 * BM);
+  const int pr = npairs - 1 - blockIdx.y;  // longest rows first over the whole grid
+  const int h = blockIdx.x % a.nq, b = blockIdx.x / a.nq;
+  const int hk = h / (a.nq / a.nkv);
+  const int qb0 = 2 * pr;                  // tile A; tile B = qb0 + 1
+  const int nkb_a = qb0 + 1, nkb_b = qb0 + 2;
+  const int row0 = b * a.S;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&pv_done[i], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_qk);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const uint32_t t_s[2] = {tmem, tmem + 128};
+  const uint32_t t_o[2] = {tmem + 256, tmem + 256 + HD};
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, 2 * L::Q_BYTES);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c)
+          tma_load_2d(sm + L::Q_OFF + t * L::Q_BYTES + c * 16384, &tm_qk, q_full, h * HD + c * 64,
+                      row0 + (qb0 + t) * BM);
+      bool ok = true;
+      for (int j = 0; j < nkb_b && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t par = ((j >> 1) & 1) ^ 1;
+        if (*abort_flag || !mbar_wait(&k_empty[st], par, a.err)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&k_full[st], L::K_BYTES);
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c)
+          tma_load_2d(sm + L::K_OFF + st * L::K_BYTES + c * 16384, &tm_qk, &k_full[st], (a.nq + hk) * HD + c * 64,
+                      row0 + j * BN);
+        if (*abort_flag || !mbar_wait(&v_empty[st], par, a.err)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[st], L::V_BYTES);
+        uint8_t* sv = sm + L::V_OFF + st * L::V_BYTES;
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+          for (int c = 0; c < HD / 64; ++c)
+            tma_load_2d(sv + i * (HD / 64) * 8192 + c * 8192, &tm_v, &v_full[st], (a.nq + a.nkv + hk) * HD + c * 64,
+                        row0 + j * BN + i * 64);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_S = idesc_bf16(BM, BN, false, false);
+      constexpr uint32_t ID_O = idesc_bf16(BM, HD, false, true);
+      const uint32_t q0 = smem_u32(sm + L::Q_OFF);
+      bool ok = mbar_wait(q_full, 0, a.err);
+      auto issue_s = [&](int t, int j) -> bool {  // S_t(j) = Q_t K_j^T
+        const int st = j & 1;
+        if (!mbar_wait(&k_full[st], (j >> 1) & 1, a.err)) return false;
+        tc_fence_after();
+        const uint32_t k0 = smem_u32(sm + L::K_OFF + st * L::K_BYTES);
+        const uint32_t qt = q0 + t * L::Q_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_bf16(t_s[t], sdesc_sw128(qt + off, 16, 1024), sdesc_sw128(k0 + off, 16, 1024), ID_S, kk != 0);
+        }
+        umma_commit(&s_full[t]);
+        // K_j is done once tile B (its later user, or its only one past tile A's last key tile) has it
+        if (t == 1 || j >= nkb_a) umma_commit(&k_empty[st]);
+        return true;
+      };
+      auto issue_pv = [&](int t, int j) -> bool {  // O_t += P_t V_j, P_t from TMEM
+        if (!mbar_wait(&p_full[t], j & 1, a.err)) return false;
+        tc_fence_after();
+        const uint32_t v0 = smem_u32(sm + L::V_OFF + (j & 1) * L::V_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint32_t vb = v0 + (kk >> 2) * (HD / 64) * 8192 + (kk & 3) * 2048;
+          umma_bf16_ta(t_o[t], t_s[t] + 8 * kk, sdesc_sw128(vb, 8192, 1024), ID_O, (j | kk) != 0);
+        }
+        umma_commit(&pv_done[t]);
+        return true;
+      };
+      if (ok) ok = issue_s(0, 0);
+      if (ok) ok = issue_s(1, 0);
+      for (int j = 0; j < nkb_b && ok && !*abort_flag; ++j) {
+        if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, a.err)) {
+          ok = false;
+          break;
+        }
+        if (j < nkb_a) {
+          if (!issue_pv(0, j)) {
+            ok = false;
+            break;
+          }
+          if (j + 1 < nkb_a && !issue_s(0, j + 1)) {
+            ok = false;
+            break;
+          }
+        }
+        if (!issue_pv(1, j)) {
+          ok = false;
+          break;
+        }
+        umma_commit(&v_empty[j & 1]);  // V_j read by both tiles' products
+        if (j + 1 < nkb_b && !issue_s(1, j + 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warps
+    const int t = (warp - 2) >> 2;           // 0: tile A, 1: tile B
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;          // row within the tile == TMEM lane
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t ts = t_s[t] + lane_off;
+    const int qb = qb0 + t;
+    const int nkb = t == 0 ? nkb_a : nkb_b;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkb; ++j) {
+      if (*abort_flag || !mbar_wait(&s_full[t], j & 1, a.err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool diag = j == qb;             // causal mask: column c > row r on the diagonal tile
+      // pass 1: row maximum
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t ra[32], rb[32];
+        tmem_ld32_async(ts + 64 * half, ra);
+        tmem_ld32_async(ts + 64 * half + 32, rb);
+        tmem_wait_ld();
+        tmem_regs(ra);
+        tmem_regs(rb);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int ca = 64 * half + i, cb = ca + 32;
+          const float va = (diag && ca > r) ? -INFINITY : __uint_as_float(ra[i]);
+          const float vb = (diag && cb > r) ? -INFINITY : __uint_as_float(rb[i]);
+          mx4[i & 3] = fmaxf(mx4[i & 3], fmaxf(va, vb));
+        }
+      }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
+      float alpha = 1.f;
+      bool rescale = false;
+      if (mx > m_used + RESCALE_THRESHOLD) {
+        alpha = (m_used == -INFINITY) ? 0.f : exp2f(m_used - mx);
+        rescale = (m_used != -INFINITY);
+        m_used = mx;
+      }
+      // O_t is not being written: PV_t(j-1) finished before S_t(j) (s_full)
+      if (__any_sync(0xffffffffu, rescale)) {
+        const float f = rescale ? alpha : 1.f;
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+          float o[32];
+          tmem_ld32(t_o[t] + lane_off + c, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= f;
+          tmem_st32(t_o[t] + lane_off + c, o);
+        }
+        tmem_st_wait();
+      }
+      // pass 2: P = exp2(s * scale_log2 - m) in bf16 over columns [16 cc, 16 cc + 16)
+      const float neg_m = -m_used;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t rc[2][32];
+      tmem_ld32_async(ts, rc[0]);
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        tmem_wait_ld();
+        tmem_regs(rc[cc & 1]);
+        if (cc < 3) tmem_ld32_async(ts + 32 * (cc + 1), rc[(cc + 1) & 1]);
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const int c = 32 * cc + i;
+          float p0 = 0.f, p1 = 0.f;
+          const float x0 = fmaf(__uint_as_float(rc[cc & 1][i]), a.scale_log2, neg_m);
+          const float x1 = fmaf(__uint_as_float(rc[cc & 1][i + 1]), a.scale_log2, neg_m);
+          if ((c & 6) == 6) {
+            p0 = exp2_fma(x0);
+            p1 = exp2_fma(x1);
+          } else {
+            p0 = ex2_approx(x0);
+            p1 = ex2_approx(x1);
+          }
+          if (diag && c > r) p0 = 0.f;
+          if (diag && c + 1 > r) p1 = 0.f;
+          rs4[(i >> 1) & 3] += p0 + p1;
+          pk[i >> 1] = pack_bf16x2(p0, p1);
+        }
+        tmem_st16u(ts + 16 * cc, pk);
+      }
+      tmem_st_wait();
+      l = l * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+    }
+    if (ok && mbar_wait(&pv_done[t], (nkb - 1) & 1, a.err)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      const long orow = (long)row0 + qb * BM + r;
+      __nv_bfloat16* op = a.out + orow * (long)a.nq * HD + h * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        float o[32];
+        tmem_ld32(t_o[t] + lane_off + c, o);
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 w;
+          w.x = pack_bf16x2(o[i] * inv, o[i + 1] * inv);
+          w.y = pack_bf16x2(o[i + 2] * inv, o[i + 3] * inv);
+          w.z = pack_bf16x2(o[i + 4] * inv, o[i + 5] * inv);
+          w.w = pack_bf16x2(o[i + 6] * inv, o[i + 7] * inv);
+          *reinterpret_cast<uint4*>(op + c + i) = w;
+        }
+      }
+      a.lse[((long)b * a.nq + h) * a.S + qb * BM + r] = (m_used + log2f(l)) / LOG2E;
+    } else {
+      *abort_flag = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -770,6 +1088,17 @@ static bool pp_enabled() {
   return v == 1;
 }
 
+// Two query tiles per CTA with P in tensor memory (attn_fwd_ws_kernel) only when
+// DTB_ATTN_FWD_WS=1: built, not yet timed on a B200.
+static bool ws_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("DTB_ATTN_FWD_WS");
+    v = (e != nullptr && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
 template <int HD>
 void fwd_tc_launch(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse, int B, int S, int nq, int nkv,
                    float scale) {
@@ -777,6 +1106,20 @@ void fwd_tc_launch(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& ls
   const long rows = (long)B * S, cols = (long)(nq + 2 * nkv) * HD;
   const CUtensorMap tqk = qkv_map(qkv.data_ptr(), rows, cols, 128);
   const CUtensorMap tv = qkv_map(qkv.data_ptr(), rows, cols, 64);
+  if (S % (2 * BM) == 0 && ws_enabled()) {
+    using LW = SmemWS<HD>;
+    static bool cfg_ws = false;
+    if (!cfg_ws) {
+      DTB_CUDA(cudaFuncSetAttribute(attn_fwd_ws_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, LW::TOTAL));
+      cfg_ws = true;
+    }
+    FwdArgs args{reinterpret_cast<__nv_bfloat16*>(o.data_ptr()), lse.data_ptr<float>(), S, nq, nkv, scale * LOG2E,
+                 dtb_error_word()};
+    attn_fwd_ws_kernel<HD><<<dim3(nq * B, S / (2 * BM), 1), 320, LW::TOTAL, at::cuda::getCurrentCUDAStream()>>>(tqk, tv,
+                                                                                                            args);
+    DTB_LAUNCH_CHECK();
+    return;
+  }
   if (S % (2 * BM) == 0 && pp_enabled()) {
     using LP = SmemPP<HD>;
     static bool cfg_pp = false;

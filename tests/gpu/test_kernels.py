@@ -627,6 +627,32 @@ def test_attention_tcgen05_backward(b, s, nq, nkv, hd):
     assert torch.equal(d_tc, native().attn_bwd(do, qkv, o, lse, b, s, nq, nkv, hd, scale))
 
 
+def test_attention_forward_two_tiles_p_in_tmem():
+    """The forward with two query tiles per CTA and P kept in tensor memory
+    (DTB_ATTN_FWD_WS=1, read once per process: run in a child process) matches the fp32
+    oracle and the default forward's log-sum-exp."""
+    import subprocess
+    import sys
+    code = ("import sys; sys.path.insert(0, %r)\n" % os.path.dirname(os.path.dirname(os.path.dirname(
+        os.path.abspath(__file__)))) + "from tests.gpu.test_kernels import _attn_fwd_ws_case\n_attn_fwd_ws_case()\n")
+    r = subprocess.run([sys.executable, "-c", code], env=dict(os.environ, DTB_ATTN_FWD_WS="1"),
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ATTN_FWD_WS_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+def _attn_fwd_ws_case():
+    for (b, s, nq, nkv, hd) in [(1, 256, 2, 2, 128), (2, 512, 4, 2, 128), (1, 1024, 8, 2, 64), (1, 768, 4, 4, 128)]:
+        qkv = _rand(b * s, (nq + 2 * nkv) * hd)
+        scale = 1 / math.sqrt(hd)
+        o, lse = native().attn_fwd(qkv, b, s, nq, nkv, hd, scale)
+        o_legacy, lse_legacy = native().attn_fwd(qkv, b, s, nq, nkv, hd, scale, legacy=True)
+        assert _rel(o, _attn_ref(qkv, b, s, nq, nkv, hd)) < 2e-2, (b, s, nq, nkv, hd)
+        assert _rel(o, o_legacy) < 2e-2, (b, s, nq, nkv, hd)
+        assert _rel(lse, lse_legacy) < 1e-4, (b, s, nq, nkv, hd)
+    assert native().device_error() == 0
+    print("ATTN_FWD_WS_OK")
+
+
 def test_attention_backward_early_s_order_same_bits(tmp_path):
     """The dK/dV kernel with the next tile's S^T issued before this tile's dK
     (DTB_ATTN_DKDV_EARLY_S=1, read once per process: run in a child process) gives the
