@@ -1,7 +1,10 @@
 """tcgen05 GEMM throughput vs torch.matmul (cuBLAS) on 7B layer shapes, all three layouts,
 and the fused epilogues against the plain store on the same shape.
 
-    python tests/performance/bench_gemm.py [--tokens 4096]
+    python tests/performance/bench_gemm.py [--tokens 4096] [--tma-epi 0|1|2]
+
+``--tma-epi`` sets the TMA-store epilogue level (0 row-per-thread stores, 1 the default,
+2 also RoPE / SwiGLU).
 
 CUDA events around 20 calls after 3 warm-ups; operands are 30-360 MB, so most of
 each call's reads miss the 126 MB L2 (no separate flush).
@@ -35,7 +38,12 @@ def tm(f, it=20):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, default=4096)
-    M = ap.parse_args().tokens
+    ap.add_argument("--tma-epi", type=int, default=None)
+    args = ap.parse_args()
+    M = args.tokens
+    if args.tma_epi is not None:
+        from build_your_own_distributed_training_b200.ops._ext import native
+        native().gemm_tma_epilogue(args.tma_epi)
     rows = []
     for (N, K) in [(12288, 4096), (4096, 4096), (22016, 4096), (4096, 11008), (32000, 4096)]:
         a = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
