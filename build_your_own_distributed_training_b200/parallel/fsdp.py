@@ -194,6 +194,14 @@ class FullyShardedModel(nn.Module):
         if getattr(self.comm, "norm_partials", False) and self.units and self.replication == 1:
             nb = max(self.comm.norm_partial_blocks(u.shard_numel) for u in self.units)
             self._norm_parts = torch.zeros(len(self.units), nb, device=self.device, dtype=torch.float32)
+        # otherwise: each unit's sums of squares [plain part, TP-replicated part] of its
+        # gradient shard, taken right after the unit's reduction (on CUDA on the communication
+        # stream, so the pass over the gradients overlaps the rest of the backward instead of
+        # following it); the same kernels and summation order as a pass after the backward
+        self._unit_ss: torch.Tensor | None = None
+        self._ss_fresh = [False] * len(self.units)
+        if self.units and self._norm_parts is None:
+            self._unit_ss = torch.zeros(len(self.units), 2, device=self.device, dtype=torch.float32)
         self._gather_all_root()
 
     # ------------------------------------------------------------------ build
@@ -323,6 +331,9 @@ class FullyShardedModel(nn.Module):
         nvtx.push(f"block{bi}.bwd")
         if not self._bwd_started:
             self._bwd_started = True
+            # gradients change from here: the norm terms of an earlier reduction are stale
+            self._norm_fresh = [False] * len(self.units)
+            self._ss_fresh = [False] * len(self.units)
             torch.autograd.Variable._execution_engine.queue_callback(self._finish_backward)
         self._ensure(bi)
         # BACKWARD_PRE: gather the previous block while this one computes its gradients
@@ -423,6 +434,18 @@ class FullyShardedModel(nn.Module):
             self._norm_fresh[u.index] = True
         else:
             self.comm.reduce_scatter_mean(u.grad_shard, u.grad, self.dp_size)
+            if self._unit_ss is not None:
+                for k, (a, b) in enumerate(self._norm_segments(u)):
+                    if b > a:
+                        self._unit_ss[u.index, k].copy_(_sumsq(u.grad_shard[a:b]))
+                self._ss_fresh[u.index] = True
+
+    def _norm_segments(self, u: FlatUnit) -> tuple[tuple[int, int], tuple[int, int]]:
+        """Shard-local ranges of the unit's plain and TP-replicated gradient entries."""
+        lo, hi = u.shard_range(self.shard_rank)
+        a, b = _clip(0, u.tp_end, lo, hi)
+        c, d = _clip(u.tp_end, u.numel, lo, hi)
+        return (a - lo, b - lo), (c - lo, d - lo)
 
     def wait_reduce(self) -> None:
         if self._is_cuda:
@@ -440,6 +463,7 @@ class FullyShardedModel(nn.Module):
     def zero_grad_buffers(self) -> None:
         """Logically zero every gradient: slices become fresh, the first writer overwrites them."""
         self._norm_fresh = [False] * len(self.units)
+        self._ss_fresh = [False] * len(self.units)
         for u in self.units:
             u.fresh.mark([(e.offset, e.numel) for e in u.entries])
 
@@ -455,20 +479,20 @@ class FullyShardedModel(nn.Module):
         """Sum of g^2 over this rank's gradient shards; TP-replicated entries weighted 1/tp.
 
         When this step's reduce-scatters left their per-block partials (NVLink transport),
-        this is one fixed-order sum over them; otherwise a pass over the shards."""
+        this is one fixed-order sum over them; otherwise the per-unit terms taken after each
+        unit's reduction (or, if a unit was not reduced since the backward began, a pass over
+        its shard) summed in unit order."""
         if self._norm_parts is not None and all(self._norm_fresh):
             from ..ops._ext import native
             return native().sum_small(self._norm_parts)
+        ready = self._unit_ss is not None and all(self._ss_fresh)
         tot = torch.zeros((), dtype=torch.float32, device=self.device)
         for u in self.units:
-            lo, hi = u.shard_range(self.shard_rank)
-            gs = u.grad_shard
-            a, b = _clip(0, u.tp_end, lo, hi)
+            (a, b), (c, d) = self._norm_segments(u)
             if b > a:
-                tot = tot + _sumsq(gs[a - lo:b - lo])
-            a, b = _clip(u.tp_end, u.numel, lo, hi)
-            if b > a:
-                tot = tot + _sumsq(gs[a - lo:b - lo]) / self.tp_size
+                tot = tot + (self._unit_ss[u.index, 0] if ready else _sumsq(u.grad_shard[a:b]))
+            if d > c:
+                tot = tot + (self._unit_ss[u.index, 1] if ready else _sumsq(u.grad_shard[c:d])) / self.tp_size
         # NO_SHARD / HYBRID_SHARD hold the same averaged shard on several dp ranks
         return tot / self.replication
 

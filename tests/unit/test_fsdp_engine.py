@@ -177,3 +177,32 @@ def test_backward_prefetch_order(single_process_pg, mode):
     i_pre = events.index(("prefetch", 1))
     i_post = events.index(("post", 2))
     assert (i_pre < i_post) if mode == "BACKWARD_PRE" else (i_pre > i_post), events
+
+
+def _norm_terms_worker(rank, world, tp):
+    """The per-unit sums of squares taken right after each unit's reduction give the same
+    norm bits as a pass over the gradient shards after the backward, and are not used once a
+    backward that reduced nothing (no_sync) has changed the gradients."""
+    cfg = tiny_config(parallel__tp_size=tp)
+    ctx = build_process_context(tp, backend="gloo", verbose=False)
+    eng = build_engine(cfg, ctx)
+    g = torch.Generator().manual_seed(3 + rank // tp)
+    toks = torch.randint(0, 256, (2, 17), generator=g)
+    _, loss = eng(toks[:, :-1], labels=toks[:, 1:])
+    loss.backward()
+    eng.wait_reduce()
+    assert eng._unit_ss is not None and all(eng._ss_fresh)
+    early = eng.grad_norm_sq_local().clone()
+    eng._ss_fresh = [False] * len(eng.units)
+    late = eng.grad_norm_sq_local()
+    assert torch.equal(early, late) and float(late) > 0
+    eng._ss_fresh = [True] * len(eng.units)
+    with eng.no_sync():
+        _, l2 = eng(toks[:, :-1], labels=toks[:, 1:])
+        l2.backward()
+    assert not any(eng._ss_fresh)
+
+
+@pytest.mark.parametrize("tp", [1, 2])
+def test_norm_terms_after_each_reduction_match_a_pass(tp):
+    run_distributed(_norm_terms_worker, 2, tp)
