@@ -14,6 +14,12 @@ pytestmark = pytest.mark.gpu
 if not torch.cuda.is_available():  # pragma: no cover - collected on CPU boxes, skipped by marker
     pytest.skip("needs a GPU", allow_module_level=True)
 
+# Kernel variants that are built but not yet the default (each behind its own switch) are
+# checked only when DTB_TEST_OPT_IN=1, so that a variant still under development cannot fail
+# a run of the default kernels.
+opt_in = pytest.mark.skipif(os.environ.get("DTB_TEST_OPT_IN") != "1",
+                            reason="opt-in kernel variant (DTB_TEST_OPT_IN=1 runs it)")
+
 from build_your_own_distributed_training_b200.ops import gemm  # noqa: E402
 from build_your_own_distributed_training_b200.ops._ext import native  # noqa: E402
 
@@ -148,6 +154,7 @@ def test_gemm_tma_epilogues_match_row_path(M, N, K):
     assert _rel(tma["st"], reft) < 1e-5
 
 
+@opt_in
 @pytest.mark.parametrize("M,hd,seq", [(512, 128, 256), (300, 64, 300)])
 def test_gemm_tma_rope_swiglu_match_row_path(M, hd, seq):
     """The RoPE and SwiGLU epilogues through TMA boxes (epilogue level 2, not yet the
@@ -627,6 +634,7 @@ def test_attention_tcgen05_backward(b, s, nq, nkv, hd):
     assert torch.equal(d_tc, native().attn_bwd(do, qkv, o, lse, b, s, nq, nkv, hd, scale))
 
 
+@opt_in
 def test_attention_forward_two_tiles_p_in_tmem():
     """The forward with two query tiles per CTA and P kept in tensor memory
     (DTB_ATTN_FWD_WS=1, read once per process: run in a child process) matches the fp32
@@ -653,6 +661,7 @@ def _attn_fwd_ws_case():
     print("ATTN_FWD_WS_OK")
 
 
+@opt_in
 def test_attention_backward_early_s_order_same_bits(tmp_path):
     """The dK/dV kernel with the next tile's S^T issued before this tile's dK
     (DTB_ATTN_DKDV_EARLY_S=1, read once per process: run in a child process) gives the
